@@ -1,0 +1,581 @@
+#!/usr/bin/env python3
+"""Benchmark of libgemm_sm100 on the configurations slang-gemm's north star names.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+One step is one call of the hot path over one batch of synthetic input (one
+gemmEx / gemmStridedBatchedEx / sgemm). The default workload is configuration
+C3 of the north star at the size the headline metric is quoted on:
+gemmEx, A and B CUDA_R_16F ~ N(0,1)*0.25, C CUDA_R_32F, CUBLAS_COMPUTE_32F,
+op N/N, M = N = K = 8192, alpha = 1, beta = 0.
+
+Rank 0 prints ONE JSON line:
+  value     whole-job TFLOP/s (TOP/s for INT8) with inputs resident in HBM,
+            device-timed with CUDA events on the launching stream, max over ranks;
+  e2e       the same metric through the host-buffer entry point gs_host_gemm_ex
+            (pinned host A/B in, C out, copies inside the timed region);
+  roofline  the tensor-core kernel against the measured B200 peak;
+  cpu_baseline  the C restatement of the reference's scalar gemmEx (oracle/)
+            timed on this host's cores on a bounded sample of the same GEMM.
+With N > 1 ranks (torchrun, NCCL), the work is sharded with no data-path
+collective: column blocks of B and C for single GEMMs, batch entries for
+batched calls, each rank holding a fixed share (weak scaling).
+
+`--impl reference` times the reference's own CPU algorithm (the oracle port of
+src/gemm.zig gemmExCuda, all host threads) on the same config and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "slang-gemm_b200")
+ORACLE_DIR = os.path.join(ROOT, "oracle")
+sys.path.insert(0, PKG)
+
+METRIC = "gemmEx TFLOPS/TOPS at 8192³ vs B200 dense peak; shader_cublas_ratio"
+
+# name -> workload. dt/ct: CUDA data types; shard: how N > 1 ranks split the work.
+CONFIGS = {
+    "c3-f16-nn": dict(api="ex", dt=2, ct=0, comp=68, op=(0, 0), m=8192, n=8192, k=8192, batch=1, alpha=1.0, beta=0.0,
+                      shard="cols", label="gemmEx C3: A,B CUDA_R_16F N(0,1)*0.25, C CUDA_R_32F, COMPUTE_32F, op N/N, "
+                                          "M=N=K=8192, alpha=1, beta=0"),
+    "c3-f16-tn": dict(api="ex", dt=2, ct=0, comp=68, op=(1, 0), m=8192, n=8192, k=8192, batch=1, alpha=1.0, beta=0.0,
+                      shard="cols", label="gemmEx C3: A,B CUDA_R_16F, C CUDA_R_32F, COMPUTE_32F, op T/N, M=N=K=8192"),
+    "c3-bf16-nn": dict(api="ex", dt=14, ct=0, comp=68, op=(0, 0), m=8192, n=8192, k=8192, batch=1, alpha=1.0,
+                       beta=0.0, shard="cols",
+                       label="gemmEx C3: A,B CUDA_R_16BF, C CUDA_R_32F, COMPUTE_32F, op N/N, M=N=K=8192"),
+    "c3-f16-nn-4096": dict(api="ex", dt=2, ct=0, comp=68, op=(0, 0), m=4096, n=4096, k=4096, batch=1, alpha=1.0,
+                           beta=0.0, shard="cols", label="gemmEx C3: f16 -> f32, op N/N, M=N=K=4096"),
+    "c5-i8-nn": dict(api="ex", dt=3, ct=10, comp=72, op=(0, 0), m=8192, n=8192, k=8192, batch=1, alpha=1.0, beta=0.0,
+                     shard="cols", label="gemmEx C5: A,B CUDA_R_8I uniform [-128,127], C CUDA_R_32I, COMPUTE_32I, "
+                                         "op N/N, M=N=K=8192, alpha=1, beta=0"),
+    "c4-f16-strided": dict(api="strided", dt=2, ct=0, comp=68, op=(0, 0), m=512, n=512, k=1024, batch=256,
+                           alpha=1.0 / 32.0, beta=0.0, shard="batch",
+                           label="gemmStridedBatchedEx C4: f16 -> f32, batch 256, M=N=512, K=1024, "
+                                 "strides MK/KN/MN, alpha=1/sqrt(K), beta=0"),
+    "c5b-i8-strided": dict(api="strided", dt=3, ct=10, comp=72, op=(0, 0), m=2048, n=2048, k=2048, batch=64,
+                           alpha=1.0, beta=0.0, shard="batch",
+                           label="gemmStridedBatchedEx C5b: s8 -> s32, batch 64, M=N=K=2048"),
+    "c2-sgemm-nn": dict(api="sgemm", dt=0, ct=0, comp=68, op=(0, 0), m=4096, n=1024, k=2048, batch=1, alpha=1.5,
+                        beta=0.5, shard="cols", label="sgemm C2: FP32 op N/N, 4096x1024x2048, alpha=1.5, beta=0.5"),
+    "c2-sgemm-tt": dict(api="sgemm", dt=0, ct=0, comp=68, op=(1, 1), m=1024, n=4096, k=512, batch=1, alpha=1.5,
+                        beta=0.5, shard="cols", label="sgemm C2: FP32 op T/T, 1024x4096x512, alpha=1.5, beta=0.5"),
+    "c1-sgemm-512": dict(api="sgemm", dt=0, ct=0, comp=68, op=(0, 0), m=512, n=512, k=512, batch=1, alpha=1.0,
+                         beta=0.0, shard="cols", label="sgemm C1: FP32 op N/N, 512^3, alpha=1, beta=0"),
+}
+ELEM = {0: 4, 2: 2, 3: 1, 10: 4, 14: 2}
+DTYPE_NAME = {0: "f32", 2: "f16", 3: "s8", 14: "bf16"}
+
+
+def load_peaks() -> dict:
+    """Roofline denominators: MEASURED_PEAKS.json (driver-written) or the pool's fallback."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16": float(d["bf16_tflops"]),
+                "bf16_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "sm_max_mhz": float(d.get("sm_max_mhz", 1965.0)), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "sm_max_mhz": 1965.0,
+                "source": "fallback"}
+
+
+def work(cfg: dict) -> tuple[float, float]:
+    """(algorithmic flops, algorithmic bytes) of one step of one rank's share."""
+    m, n, k, b = cfg["m"], cfg["n"], cfg["k"], cfg["batch"]
+    es, ec = ELEM[cfg["dt"]], ELEM[cfg["ct"]]
+    flops = 2.0 * m * n * k * b
+    byts = b * (m * k * es + k * n * es + m * n * ec * (2 if cfg["beta"] != 0 else 1))
+    return flops, float(byts)
+
+
+def roofline_of(cfg: dict, flops: float, byts: float, ms_per_launch: float, peaks: dict, traffic) -> dict:
+    """Tensor-core bound for the 8192^3 GEMMs; HBM bound for the batched f16 config; FFMA for sgemm."""
+    ai = flops / byts
+    if cfg["api"] == "sgemm":
+        peak = 148 * 128 * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12
+        achieved = flops / (ms_per_launch * 1e-3) / 1e12
+        return {"bound": "ffma", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": "nominal 148 SM x 128 FP32 lanes x 2 x max SM clock (no measured FFMA peak)"}
+    tensor_peak = peaks["bf16"] * (2.0 if cfg["dt"] == 3 else 1.0)
+    ridge = tensor_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    if ai < ridge:
+        achieved = byts / (ms_per_launch * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                "peak_source": f"{peaks['source']} HBM copy bandwidth"}
+    achieved = flops / (ms_per_launch * 1e-3) / 1e12
+    src = f"{peaks['source']} cuBLAS bf16 burst" + (" x2 for INT8 (dense INT8 rate is twice BF16 on B200)"
+                                                    if cfg["dt"] == 3 else "")
+    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(tensor_peak, 1),
+            "unit": "TOP/s" if cfg["dt"] == 3 else "TFLOP/s", "frac": round(achieved / tensor_peak, 4),
+            "traffic": traffic, "peak_source": src}
+
+
+def committed_traffic(name: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        return json.load(open(p)).get(name)
+    except Exception:
+        return None
+
+
+# ---- clock sampling during the timed region --------------------------------
+
+class ClockSampler:
+    """Samples the SM clock and the active clock-event reasons through NVML every ~20 ms."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int):
+        self.samples: list[int] = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            self._sample_once()
+            self._stop.wait(0.02)
+
+    def _sample_once(self):
+        nv = self._nv
+        if nv is None:
+            return
+        try:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+            self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        except Exception:
+            pass
+
+    def start(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self) -> dict:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+            self._sample_once()
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        s = sorted(self.samples)
+        names = [v for bit, v in self.REASONS.items() if self.reasons & bit and bit != 0x1]
+        return {"sm_mhz": s[len(s) // 2], "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(s)}
+
+
+# ---- distributed plumbing -----------------------------------------------------
+
+def dist_setup(n_gpus: int):
+    import torch
+
+    if n_gpus <= 1 or "RANK" not in os.environ:
+        torch.cuda.set_device(0)
+        return 0, 1, 0, None
+    import datetime
+
+    import torch.distributed as dist
+
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
+    return dist.get_rank(), dist.get_world_size(), local, dist
+
+
+def max_over_ranks(dist, value: float) -> float:
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    import torch
+
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---- our implementation ----------------------------------------------------------
+
+def rank_share(cfg: dict, rank: int, world: int, scaling: str) -> dict:
+    """This rank's share: weak scaling keeps one configuration's worth of work per rank."""
+    import gemm_sm100 as gs
+
+    c = dict(cfg)
+    if world == 1:
+        return c
+    if cfg["shard"] == "batch":
+        total = cfg["batch"] * (world if scaling == "weak" else 1)
+        cuts = gs.plan_shards(total, world, 1)
+        c["batch"] = cuts[rank + 1] - cuts[rank]
+    else:
+        total = cfg["n"] * (world if scaling == "weak" else 1)
+        cuts = gs.plan_shards(total, world, 256)
+        c["n"] = cuts[rank + 1] - cuts[rank]
+    return c
+
+
+def make_inputs(cfg: dict, seed: int):
+    """Seeded synthetic operands on the current device (configuration value distributions)."""
+    import torch
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    m, n, k, b = cfg["m"], cfg["n"], cfg["k"], cfg["batch"]
+    dt = cfg["dt"]
+    na, nb, nc = m * k * b, k * n * b, m * n * b
+    if dt == 3:
+        A = torch.randint(-128, 128, (na,), generator=g, device="cuda", dtype=torch.int16).to(torch.int8)
+        B = torch.randint(-128, 128, (nb,), generator=g, device="cuda", dtype=torch.int16).to(torch.int8)
+        C = torch.zeros(nc, device="cuda", dtype=torch.int32)
+    elif dt == 0:
+        A = torch.rand(na, generator=g, device="cuda") * 2 - 1
+        B = torch.rand(nb, generator=g, device="cuda") * 2 - 1
+        C = torch.rand(nc, generator=g, device="cuda") * 2 - 1
+    else:
+        tdt = torch.float16 if dt == 2 else torch.bfloat16
+        A = (torch.randn(na, generator=g, device="cuda") * 0.25).to(tdt)
+        B = (torch.randn(nb, generator=g, device="cuda") * 0.25).to(tdt)
+        C = torch.zeros(nc, device="cuda", dtype=torch.float32)
+    return A, B, C
+
+
+def call(h, cfg: dict, A, B, C):
+    """One step through the cuBLAS-shaped device entry point."""
+    m, n, k, b = cfg["m"], cfg["n"], cfg["k"], cfg["batch"]
+    ta, tb = cfg["op"]
+    lda = m if ta == 0 else k
+    ldb = k if tb == 0 else n
+    if cfg["api"] == "sgemm":
+        h.sgemm(ta, tb, m, n, k, cfg["alpha"], A, lda, B, ldb, cfg["beta"], C, m)
+    elif cfg["api"] == "strided":
+        h.gemm_strided_batched_ex(ta, tb, m, n, k, cfg["alpha"], A, cfg["dt"], lda, m * k, B, cfg["dt"], ldb, k * n,
+                                  cfg["beta"], C, cfg["ct"], m, m * n, b, cfg["comp"])
+    else:
+        h.gemm_ex(ta, tb, m, n, k, cfg["alpha"], A, cfg["dt"], lda, B, cfg["dt"], ldb, cfg["beta"], C, cfg["ct"], m,
+                  cfg["comp"])
+
+
+def call_host(h, cfg: dict, Ah, Bh, Ch):
+    """One step through the host-buffer entry point (gs_host_gemm_ex): H2D, compute, D2H."""
+    m, n, k, b = cfg["m"], cfg["n"], cfg["k"], cfg["batch"]
+    ta, tb = cfg["op"]
+    lda = m if ta == 0 else k
+    ldb = k if tb == 0 else n
+    h.host_gemm_ex(ta, tb, m, n, k, cfg["alpha"], Ah, cfg["dt"], lda, Bh, cfg["dt"], ldb, cfg["beta"], Ch, cfg["ct"],
+                   m, cfg["comp"], batch=b)
+
+
+def l2_flush_needed(cfg: dict) -> bool:
+    m, n, k, b = cfg["m"], cfg["n"], cfg["k"], cfg["batch"]
+    largest = max(m * k, k * n) * b * ELEM[cfg["dt"]]
+    return largest <= 126 * 2 ** 20
+
+
+def run_ours(args, cfg_name: str) -> None:
+    import torch
+
+    import gemm_sm100 as gs
+
+    cfg0 = CONFIGS[cfg_name]
+    rank, world, local, dist = dist_setup(args.gpus)
+    cfg = rank_share(cfg0, rank, world, args.scaling)
+    peaks = load_peaks()
+    stream = torch.cuda.current_stream()
+    h = gs.Handle(stream=stream)
+    A, B, C = make_inputs(cfg, seed=1234 + rank)
+    flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device="cuda") if l2_flush_needed(cfg) else None
+
+    def step():
+        if flush is not None:
+            flush.zero_()
+        call(h, cfg, A, B, C)
+
+    for _ in range(args.warmup):
+        step()
+    barrier(dist)
+    sampler = ClockSampler(local)
+    launches0 = h.launch_count()
+    sampler.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kernel_ms = 0.0
+    if flush is None:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            call(h, cfg, A, B, C)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        elapsed = ev0.elapsed_time(ev1)
+        kernel_ms = elapsed / max(1, args.steps)
+    else:
+        # L2 is flushed between steps; the GEMM launch alone is timed per step.
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        ev0.record(stream)
+        for s0, s1 in evs:
+            flush.zero_()
+            s0.record(stream)
+            call(h, cfg, A, B, C)
+            s1.record(stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        kernel_ms = sum(s0.elapsed_time(s1) for s0, s1 in evs) / max(1, args.steps)
+        elapsed = kernel_ms * args.steps
+    clocks = sampler.stop()
+    launches = h.launch_count() - launches0
+    dev_err = h.device_error()
+    barrier(dist)
+    max_elapsed = max_over_ranks(dist, elapsed)
+    max_kernel_ms = max_over_ranks(dist, kernel_ms)
+    flops_rank, bytes_rank = work(cfg)
+    total_flops = flops_rank * world if dist is None else max_over_ranks(dist, 0.0) * 0 + flops_rank * world
+    ms_per_step = max_elapsed / max(1, args.steps)
+    value = total_flops / (ms_per_step * 1e-3) / 1e12
+
+    # ---- end to end through the host-buffer entry point ----
+    Ah = A.cpu().pin_memory()
+    Bh = B.cpu().pin_memory()
+    Ch = C.cpu().pin_memory()
+    e2e_steps = max(1, min(args.steps, 20))
+    call_host(h, cfg, Ah, Bh, Ch)  # warm the staging buffers
+    barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        call_host(h, cfg, Ah, Bh, Ch)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1)) / e2e_steps
+    e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
+    h2d = A.numel() * A.element_size() + B.numel() * B.element_size()
+    c_dense = True
+    if cfg["beta"] != 0 or not c_dense:
+        h2d += C.numel() * C.element_size()
+    d2h = C.numel() * C.element_size()
+
+    roof = roofline_of(cfg, flops_rank, bytes_rank, max_kernel_ms, peaks, committed_traffic(cfg_name))
+    unit = "TOP/s" if cfg["dt"] == 3 else "TFLOP/s"
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": unit,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak" if world > 1 and args.scaling == "weak" else ("strong" if world > 1 else "weak"),
+        "vs_baseline": None,
+        "dtype": DTYPE_NAME[cfg["dt"]],
+        "data": "synthetic (seeded torch generator; value distributions of the configuration)",
+        "config": {"workload": cfg0["label"], "name": cfg_name,
+                   "per_rank": {"m": cfg["m"], "n": cfg["n"], "k": cfg["k"], "batch": cfg["batch"]},
+                   "sharding": "none" if world == 1 else (f"{cfg0['shard']} split, {args.scaling} scaling, "
+                                                          "no data-path collective"),
+                   "l2": "flushed (256 MiB write) before every step" if flush is not None
+                   else "inputs larger than L2 (126 MB)"},
+        "e2e": {"value": round(e2e_value, 2), "unit": unit, "h2d_bytes_per_step": h2d * world,
+                "d2h_bytes_per_step": d2h * world, "ms_per_step": round(e2e_ms, 3),
+                "path": "gs_host_gemm_ex (pinned host buffers; H2D, kernel, D2H, stream sync per step)"},
+        "roofline": roof,
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+        "device_error_word": dev_err,
+        "kernels": h.last_kernels(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg0, budget_s=args.cpu_seconds)
+    if args.cublas and rank == 0:
+        line["cublas"] = cublas_compare(cfg, A, B, args.steps, args.warmup)
+    h.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cublas_compare(cfg: dict, A, B, steps: int, warmup: int) -> dict:
+    """cuBLAS (through torch) on the same operands, for the shader_cublas_ratio column."""
+    import torch
+
+    m, n, k = cfg["m"], cfg["n"], cfg["k"]
+    if cfg["api"] != "ex" or cfg["op"] != (0, 0) or cfg["dt"] == 3:
+        return {"note": "cuBLAS comparison implemented for f16/bf16 N/N gemmEx only"}
+    a = A.view(k, m)  # column-major m x k == row-major k x m
+    b = B.view(n, k)
+    out = torch.empty(n, m, device="cuda", dtype=torch.float32)
+    try:
+        fn = lambda: torch.mm(b, a, out_dtype=torch.float32, out=out)  # noqa: E731
+        fn()
+        kind = "torch.mm(out_dtype=float32)"
+    except Exception:
+        fn = lambda: torch.mm(b, a)  # noqa: E731
+        kind = "torch.mm (f16 output)"
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"ms": round(ms, 4), "tflops": round(2.0 * m * n * k / ms / 1e9, 1), "call": kind}
+
+
+# ---- CPU legs: the reference's scalar algorithm (oracle port) ----------------------
+
+def _oracle():
+    sys.path.insert(0, ORACLE_DIR)
+    import oracle
+
+    return oracle
+
+
+def _cpu_sample(cfg: dict, cols: int, threads: int, seed: int = 7) -> float:
+    """Seconds for the oracle to compute `cols` full columns of C (all M rows, full K)."""
+    import numpy as np
+
+    orc = _oracle()
+    rng = np.random.default_rng(seed)
+    m, k = cfg["m"], cfg["k"]
+    ta, tb = cfg["op"]
+    dt, ct = cfg["dt"], cfg["ct"]
+    if not hasattr(_cpu_sample, "cache") or _cpu_sample.cache[0] != (m, k, dt):
+        if dt == 3:
+            a = rng.integers(-128, 128, m * k).astype(np.int8)
+        elif dt == 0:
+            a = rng.uniform(-1, 1, m * k).astype(np.float32)
+        else:
+            a = orc.randn_lowp(rng, m * k, dt)
+        _cpu_sample.cache = ((m, k, dt), a)
+    a = _cpu_sample.cache[1]
+    if dt == 3:
+        b = rng.integers(-128, 128, k * cols).astype(np.int8)
+        c = np.zeros(m * cols, np.int32)
+    elif dt == 0:
+        b = rng.uniform(-1, 1, k * cols).astype(np.float32)
+        c = rng.uniform(-1, 1, m * cols).astype(np.float32)
+    else:
+        b = orc.randn_lowp(rng, k * cols, dt)
+        c = np.zeros(m * cols, np.float32)
+    lda = m if ta == 0 else k
+    ldb = k if tb == 0 else cols
+    t0 = time.perf_counter()
+    if cfg["api"] == "sgemm":
+        rc = orc.sgemm_strided_batched_mt(orc.COL_MAJOR, ta, tb, m, cols, k, cfg["alpha"], a, lda, 0, b, ldb, 0,
+                                          cfg["beta"], c, m, 0, 1, threads)
+    else:
+        rc = orc.gemm_ex(ta, tb, m, cols, k, cfg["alpha"], a, dt, lda, b, dt, ldb, cfg["beta"], c, ct, m,
+                         compute_type=cfg["comp"], threads=threads)
+    dt_s = time.perf_counter() - t0
+    assert rc == orc.OK
+    return dt_s
+
+
+def _cpu_plan(cfg: dict, threads: int, budget_s: float) -> tuple[int, float]:
+    """Columns per sample so that one sample takes about budget_s seconds."""
+    t1 = _cpu_sample(cfg, threads, threads)
+    per = max(1, int(budget_s / max(t1, 1e-6)))
+    return threads * per, t1
+
+
+def cpu_baseline(cfg: dict, budget_s: float = 12.0) -> dict:
+    """The C restatement of the reference's scalar gemmExCuda (src/gemm.zig:671-706), all host cores."""
+    threads = os.cpu_count() or 1
+    cols, _ = _cpu_plan(cfg, threads, budget_s)
+    cols = min(cols, cfg["n"])
+    secs = _cpu_sample(cfg, cols, threads)
+    flops = 2.0 * cfg["m"] * cols * cfg["k"]
+    unit = "TOP/s" if cfg["dt"] == 3 else "TFLOP/s"
+    return {"value": flops / secs / 1e12, "unit": unit, "cores": threads, "kind": "port",
+            "sample": f"{cols} of {cfg['n']} output columns (all {cfg['m']} rows, full K={cfg['k']}) of one "
+                      f"{cfg['m']}x{cfg['n']}x{cfg['k']} GEMM, {secs:.1f} s, {threads} threads "
+                      "(oracle/gemm_oracle.c, the scalar f64-accumulating loop of src/gemm.zig)"}
+
+
+def run_reference(args, cfg_name: str) -> None:
+    """--impl reference: the reference's CPU algorithm on this host, same config / metric / unit."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return  # only rank 0 runs and prints under torchrun
+    cfg = CONFIGS[cfg_name]
+    threads = os.cpu_count() or 1
+    total_steps = args.steps + args.warmup
+    per_step_budget = max(0.5, args.ref_seconds / max(1, total_steps))
+    cols, _ = _cpu_plan(cfg, threads, per_step_budget)
+    cols = min(cols, cfg["n"])
+    for _ in range(args.warmup):
+        _cpu_sample(cfg, cols, threads)
+    t = 0.0
+    for _ in range(args.steps):
+        t += _cpu_sample(cfg, cols, threads)
+    flops = 2.0 * cfg["m"] * cols * cfg["k"] * args.steps
+    value = flops / t / 1e12
+    unit = "TOP/s" if cfg["dt"] == 3 else "TFLOP/s"
+    sample = (f"{cols} of {cfg['n']} output columns per step (all {cfg['m']} rows, full K={cfg['k']}), "
+              f"{threads} threads, oracle/gemm_oracle.c (C restatement of src/gemm.zig gemmExCuda; "
+              "the Zig reference itself cannot be built here)")
+    line = {
+        "metric": METRIC, "value": value, "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * t / max(1, args.steps), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_NAME[cfg["dt"]], "data": "synthetic",
+        "config": {"workload": cfg["label"], "name": cfg_name},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c3-f16-nn", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--cublas", action="store_true", help="also time cuBLAS (torch.mm) on the same operands")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the cpu_baseline sample")
+    ap.add_argument("--ref-seconds", type=float, default=90.0, help="target total length of --impl reference")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args, args.config)
+    else:
+        run_ours(args, args.config)
+
+
+if __name__ == "__main__":
+    main()

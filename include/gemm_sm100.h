@@ -1,0 +1,214 @@
+/*
+ * gemm_sm100.h -- C ABI of libgemm_sm100, a B200 (sm_100a) GEMM backend that
+ * sits behind slang-gemm's cuBLAS-shaped API.
+ *
+ * Conventions (identical to cuBLAS and to slang-gemm's src/cublas.zig):
+ *  - Matrices are column-major. Element (r, c) of a matrix with leading
+ *    dimension ld lives at base[r + c*ld].
+ *  - op values: GS_OP_N = 0, GS_OP_T = 1, GS_OP_C = 2 (src/cublas.zig:14-18).
+ *    For real types GS_OP_C is identical to GS_OP_T.
+ *  - Data / compute / algo enums carry CUDA's integer values
+ *    (src/gemm.zig:14-113, pinned by tests/gemm_classic_extended.zig:6-16).
+ *  - alpha and beta are HOST pointers whose type follows compute_type:
+ *    float for GS_COMPUTE_32F*, int32_t for GS_COMPUTE_32I*, a uint16_t holding
+ *    f16 bits for GS_COMPUTE_16F.
+ *  - A, B, C (and the batched pointer arrays) are DEVICE pointers owned by the
+ *    caller. All calls are asynchronous and ordered on the handle's stream.
+ *  - beta == 0 means C is not read (cuBLAS semantics).
+ *  - In strided-batched calls a stride of 0 re-uses the same matrix for every
+ *    batch entry (cuBLAS semantics). The host-buffer mirror gs_host_gemm_ex
+ *    instead follows src/gemm.zig, where 0 means "one matrix extent".
+ *  - A handle is not thread-safe; use one handle per host thread.
+ *
+ * Return codes are cuBLAS's status values (cublasStatus_t).
+ */
+#ifndef GEMM_SM100_H
+#define GEMM_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GS_VERSION_MAJOR 0
+#define GS_VERSION_MINOR 1
+
+typedef enum gs_status {
+    GS_STATUS_SUCCESS = 0,
+    GS_STATUS_NOT_INITIALIZED = 1,
+    GS_STATUS_ALLOC_FAILED = 3,
+    GS_STATUS_INVALID_VALUE = 7,
+    GS_STATUS_ARCH_MISMATCH = 8,
+    GS_STATUS_EXECUTION_FAILED = 13,
+    GS_STATUS_INTERNAL_ERROR = 14,
+    GS_STATUS_NOT_SUPPORTED = 15
+} gs_status;
+
+enum { GS_OP_N = 0, GS_OP_T = 1, GS_OP_C = 2 };
+
+/* cudaDataType values (src/gemm.zig:14-49); the ones this backend computes on. */
+enum {
+    GS_R_32F = 0, GS_R_64F = 1, GS_R_16F = 2, GS_R_8I = 3, GS_R_32I = 10, GS_R_16BF = 14
+};
+
+/* cublasComputeType_t values (src/gemm.zig:53-67). */
+enum {
+    GS_COMPUTE_16F = 64, GS_COMPUTE_16F_PEDANTIC = 65,
+    GS_COMPUTE_32F = 68, GS_COMPUTE_32F_PEDANTIC = 69,
+    GS_COMPUTE_32F_FAST_16F = 74, GS_COMPUTE_32F_FAST_16BF = 75, GS_COMPUTE_32F_FAST_TF32 = 77,
+    GS_COMPUTE_64F = 70, GS_COMPUTE_64F_PEDANTIC = 71,
+    GS_COMPUTE_32I = 72, GS_COMPUTE_32I_PEDANTIC = 73
+};
+
+/* cublasGemmAlgo_t: accepted and ignored, as src/gemm.zig:687 ignores it. */
+enum { GS_GEMM_DEFAULT = -1, GS_GEMM_DEFAULT_TENSOR_OP = 99 };
+
+/* Row/column-major selector of the host-buffer mirror (src/gemm.zig:3-6). */
+enum { GS_LAYOUT_ROW_MAJOR = 0, GS_LAYOUT_COL_MAJOR = 1 };
+
+typedef struct gs_context *gs_handle;
+
+/* ---------------------------------------------------------------------- */
+/* Handle management. Replaces cublas.Context (src/cublas.zig:78-90).      */
+/* ---------------------------------------------------------------------- */
+
+/* Creates a handle bound to the current CUDA device and the default stream.
+ * Returns GS_STATUS_ARCH_MISMATCH when the device is not compute capability 10.0. */
+gs_status gs_create(gs_handle *handle);
+gs_status gs_destroy(gs_handle handle);
+/* stream is a cudaStream_t (NULL = legacy default stream). */
+gs_status gs_set_stream(gs_handle handle, void *stream);
+gs_status gs_get_stream(gs_handle handle, void **stream);
+/* Static, NUL-terminated name of a status value. */
+const char *gs_status_name(gs_status status);
+/* Human-readable detail of the last non-success status returned on this handle. */
+const char *gs_last_error(gs_handle handle);
+/* Bit set of kernels the last call launched (GS_KERNEL_* below); for tests/benchmarks. */
+uint32_t gs_last_kernels(gs_handle handle);
+/* Total number of kernel launches issued through this handle. */
+uint64_t gs_launch_count(gs_handle handle);
+/* Synchronises the handle's stream and returns the device error word that the
+ * kernels' bounded waits write (0 = no error; bit 0 = a pipeline wait timed
+ * out, bits 8..15 = where). The word is sticky for the handle's lifetime. */
+gs_status gs_device_error(gs_handle handle, uint32_t *word);
+
+enum {
+    GS_KERNEL_TC_F16 = 1u << 0,   /* tcgen05 kind::f16, f16 operands */
+    GS_KERNEL_TC_BF16 = 1u << 1,  /* tcgen05 kind::f16, bf16 operands */
+    GS_KERNEL_TC_I8 = 1u << 2,    /* tcgen05 kind::i8 */
+    GS_KERNEL_FFMA = 1u << 3,     /* register-blocked FFMA sgemm */
+    GS_KERNEL_SIMT = 1u << 4,     /* generic CUDA-core kernel for operands TMA cannot address */
+    GS_KERNEL_SCALE = 1u << 5,    /* C = beta*C for k == 0 */
+    GS_KERNEL_TMAP = 1u << 6      /* device-side tensor-map builder (pointer-array batches) */
+};
+
+/* ---------------------------------------------------------------------- */
+/* cuBLAS-shaped device entry points                                       */
+/* ---------------------------------------------------------------------- */
+
+/* FP32 SGEMM, FFMA path. Replaces cublas.sgemm (src/cublas.zig:171-173) behind
+ * gemm.sgemm (src/gemm.zig:286-317). */
+gs_status gs_sgemm(gs_handle handle, int transa, int transb, int m, int n, int k,
+                   const float *alpha, const float *A, int lda, const float *B, int ldb,
+                   const float *beta, float *C, int ldc);
+
+/* Strided-batched SGEMM. Replaces cublas.sgemmStridedBatched
+ * (src/cublas.zig:195-197) behind gemm.sgemmStridedBatched (src/gemm.zig:479-481). */
+gs_status gs_sgemm_strided_batched(gs_handle handle, int transa, int transb, int m, int n, int k,
+                                   const float *alpha, const float *A, int lda, long long strideA,
+                                   const float *B, int ldb, long long strideB, const float *beta,
+                                   float *C, int ldc, long long strideC, int batchCount);
+
+/* FP16 in / FP16 out with FP32 accumulation and f16 alpha/beta (bits), as
+ * gemm.hgemm (src/gemm.zig:438-477). tcgen05 path. */
+gs_status gs_hgemm(gs_handle handle, int transa, int transb, int m, int n, int k,
+                   const uint16_t *alpha, const uint16_t *A, int lda, const uint16_t *B, int ldb,
+                   const uint16_t *beta, uint16_t *C, int ldc);
+
+/* Typed GEMM. Replaces cublas.gemmEx (src/cublas.zig:227-229, RawGemmExDesc
+ * :243-266) behind gemm.gemmEx (src/gemm.zig:546-576). Supported combinations:
+ *   A,B = R_16F,  C = R_32F or R_16F,  compute 32F / 32F_FAST_16F / 32F_PEDANTIC   (tcgen05)
+ *   A,B = R_16BF, C = R_32F or R_16BF, compute 32F / 32F_FAST_16BF / 32F_PEDANTIC  (tcgen05)
+ *   A,B = R_16F,  C = R_16F,           compute 16F (alpha/beta f16 bits)           (tcgen05)
+ *   A,B = R_8I,   C = R_32I,           compute 32I / 32I_PEDANTIC                  (tcgen05)
+ *   A,B,C = R_32F,                     compute 32F / 32F_PEDANTIC                  (FFMA)
+ * Anything else returns GS_STATUS_NOT_SUPPORTED. INT8 requires k <= 131071 so
+ * that the s32 accumulator cannot overflow. */
+gs_status gs_gemm_ex(gs_handle handle, int transa, int transb, int m, int n, int k,
+                     const void *alpha, const void *A, int Atype, int lda,
+                     const void *B, int Btype, int ldb, const void *beta,
+                     void *C, int Ctype, int ldc, int computeType, int algo);
+
+/* Strided-batched typed GEMM. Replaces cublas.gemmStridedBatchedEx
+ * (src/cublas.zig:235-237) behind gemm.gemmStridedBatchedEx (src/gemm.zig:632-634). */
+gs_status gs_gemm_strided_batched_ex(gs_handle handle, int transa, int transb, int m, int n, int k,
+                                     const void *alpha, const void *A, int Atype, int lda, long long strideA,
+                                     const void *B, int Btype, int ldb, long long strideB,
+                                     const void *beta, void *C, int Ctype, int ldc, long long strideC,
+                                     int batchCount, int computeType, int algo);
+
+/* Pointer-array batched typed GEMM; Aarray/Barray/Carray are DEVICE arrays of
+ * device pointers, as with cuBLAS. Replaces cublas.gemmBatchedEx
+ * (src/cublas.zig:239-241, RawGemmBatchedExDesc :268-288) behind
+ * gemm.gemmBatchedEx (src/gemm.zig:636-663). */
+gs_status gs_gemm_batched_ex(gs_handle handle, int transa, int transb, int m, int n, int k,
+                             const void *alpha, const void *const Aarray[], int Atype, int lda,
+                             const void *const Barray[], int Btype, int ldb, const void *beta,
+                             void *const Carray[], int Ctype, int ldc, int batchCount,
+                             int computeType, int algo);
+
+/* Validates a strided-batched typed GEMM exactly as gs_gemm_strided_batched_ex
+ * does (same status codes) and reports in *kernel the GS_KERNEL_* bit it would
+ * launch (0 for a no-op). Pure host logic: touches no device and needs no
+ * handle, so callers can query the dispatch decision up front. */
+gs_status gs_plan_gemm_strided_batched_ex(int transa, int transb, int m, int n, int k, const void *A, int Atype,
+                                          int lda, long long strideA, const void *B, int Btype, int ldb,
+                                          long long strideB, const void *C, int Ctype, int ldc, long long strideC,
+                                          int batchCount, int computeType, uint32_t *kernel);
+
+/* ---------------------------------------------------------------------- */
+/* Host-buffer mirror of gemm.gemmEx                                       */
+/* ---------------------------------------------------------------------- */
+
+/* Mirrors ExDesc (src/gemm.zig:236-261): host byte buffers with their lengths,
+ * row- or column-major layout, f64 complex alpha/beta (only .re is used by the
+ * real types computed here) and src/gemm.zig's stride convention (0 = extent). */
+typedef struct gs_ex_desc {
+    int op_a, op_b;
+    size_t m, n, k;
+    double alpha_re, alpha_im;
+    const void *a; size_t a_len; int a_type; size_t lda;
+    const void *b; size_t b_len; int b_type; size_t ldb;
+    double beta_re, beta_im;
+    void *c; size_t c_len; int c_type; size_t ldc;
+    int compute_type;
+    int layout;
+    size_t batch_count;
+    size_t stride_a, stride_b, stride_c;
+    int algo;
+} gs_ex_desc;
+
+/* Drop-in for gemm.gemmEx / gemm.gemmStridedBatchedEx over HOST buffers
+ * (src/gemm.zig:546, :632): validates like validateByteSliceLen
+ * (src/gemm.zig:769-775), copies A, B (and C when beta != 0) to the device,
+ * runs the device path on the handle's stream, copies C back and synchronises.
+ * Device staging buffers are owned and reused by the handle. */
+gs_status gs_host_gemm_ex(gs_handle handle, const gs_ex_desc *desc);
+
+/* ---------------------------------------------------------------------- */
+/* Multi-GPU sharding plan (pure host logic)                               */
+/* ---------------------------------------------------------------------- */
+
+/* Splits `units` (batch entries, or columns of B and C) over `parts` devices
+ * as [floor(g*units/parts), floor((g+1)*units/parts)), rounding interior cut
+ * points down to a multiple of `align` (1 = no rounding). Writes parts+1
+ * offsets into `offsets`. Used by the batch split of strided / pointer-array
+ * calls and by the column split of one large GEMM. */
+gs_status gs_plan_shards(long long units, int parts, long long align, long long *offsets);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GEMM_SM100_H */

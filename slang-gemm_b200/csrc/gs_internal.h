@@ -1,0 +1,89 @@
+// gs_internal.h -- shared declarations between the C-ABI layer and the kernels.
+#pragma once
+#include <cstdint>
+#include <string>
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/gemm_sm100.h"
+
+namespace gs {
+
+// Element / output kinds the kernels are specialised on.
+enum InKind { IN_F16 = 0, IN_BF16 = 1, IN_I8 = 2, IN_F32 = 3 };
+enum OutKind { OUT_F32 = 0, OUT_I32 = 1, OUT_F16 = 2, OUT_BF16 = 3 };
+
+// Epilogue scalars. Which fields are used depends on the output / compute kind.
+struct Epilogue {
+    float alpha_f, beta_f;    // f32 compute (16F compute is widened to f32)
+    int32_t alpha_i, beta_i;  // 32I compute
+    int beta_zero;            // beta == 0: C is not read
+    int identity;             // alpha == 1 and beta == 0: store the accumulator as is
+};
+
+// One (possibly batched) GEMM as the kernels see it, column-major, after the
+// C-ABI layer has validated it. Pointers are device pointers.
+struct GemmDesc {
+    int trans_a, trans_b;     // 0 = N, 1 = T (C is folded into T for real types)
+    int m, n, k;
+    int batch;
+    InKind in_kind;
+    OutKind out_kind;
+    const void *A; long long lda, stride_a;
+    const void *B; long long ldb, stride_b;
+    void *C; long long ldc, stride_c;
+    Epilogue ep;
+};
+
+// Kernel selection made by plan_gemm (pure host logic, no device calls).
+struct Plan {
+    uint32_t kernel;          // one GS_KERNEL_* bit
+};
+
+// Host-side context behind gs_handle.
+struct Context {
+    int device = -1;
+    int sm_count = 0;
+    cudaStream_t stream = nullptr;
+    uint32_t *dev_err = nullptr;      // [0] error word of bounded waits, [1] pointer-array misalignment flag
+    uint32_t last_kernels = 0;
+    uint64_t launches = 0;
+    std::string last_error;
+    // staging buffers of the host-buffer mirror (gs_host_gemm_ex)
+    void *stage = nullptr;
+    size_t stage_bytes = 0;
+    // device copy of tensor maps for pointer-array batches
+    void *tmap_buf = nullptr;
+    size_t tmap_bytes = 0;
+};
+
+// Validation + kernel choice for a strided (or single) GEMM; no device calls.
+gs_status plan_gemm(const GemmDesc &d, Plan *plan, std::string *why);
+
+// Launchers (return cudaSuccess or the launch error).
+cudaError_t launch_tc(Context &ctx, const GemmDesc &d);
+cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *const *a_arr,
+                                const void *const *b_arr, void *const *c_arr);
+cudaError_t launch_ffma(Context &ctx, const GemmDesc &d);
+cudaError_t launch_simt(Context &ctx, const GemmDesc &d, const void *const *a_arr,
+                        const void *const *b_arr, void *const *c_arr);
+cudaError_t launch_scale(Context &ctx, const GemmDesc &d, void *const *c_arr);
+// CUDA-core pointer-array GEMM that does its work only when *flag != 0.
+cudaError_t launch_simt_if_flag(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
+                                void *const *c_arr, const uint32_t *flag);
+
+// Tensor-map encoder obtained from the driver at run time.
+bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t dim0,
+                    uint64_t dim1, uint64_t dim2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                    uint32_t box0, uint32_t box1, std::string *why);
+
+size_t in_elem_size(InKind k);
+size_t out_elem_size(OutKind k);
+
+}  // namespace gs
+
+// The object behind gs_handle.
+struct gs_context {
+    gs::Context ctx;
+};

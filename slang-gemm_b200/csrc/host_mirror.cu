@@ -1,0 +1,187 @@
+// host_mirror.cu -- gs_host_gemm_ex: the host-buffer counterpart of
+// slang-gemm's gemm.gemmEx / gemm.gemmStridedBatchedEx (src/gemm.zig:546-576,
+// :632-634, :671-706). It takes the same ExDesc fields (host byte slices with
+// lengths, row- or column-major layout, stride 0 = one matrix extent),
+// validates them like validateByteSliceLen (src/gemm.zig:769-775), stages the
+// operands in device memory owned by the handle and runs the device path.
+#include <cmath>
+#include <cstring>
+#include <string>
+
+#include "gs_internal.h"
+
+namespace {
+
+size_t type_size(int t) {
+    switch (t) {
+    case GS_R_16F: case GS_R_16BF: return 2;
+    case GS_R_32F: case GS_R_32I: return 4;
+    case GS_R_8I: return 1;
+    case GS_R_64F: return 8;
+    default: return 0;
+    }
+}
+
+// matrixExtent with matrixLayout(layout, ld) (src/gemm.zig:165-170, :708-711).
+size_t extent(int layout, size_t ld, size_t rows, size_t cols) {
+    if (rows == 0 || cols == 0) return 0;
+    if (layout == GS_LAYOUT_ROW_MAJOR) return (rows - 1) * ld + (cols - 1) + 1;
+    return (rows - 1) + (cols - 1) * ld + 1;
+}
+
+// validateByteSliceLen (src/gemm.zig:769-775); `stride` already resolved.
+gs_status check_len(size_t len, size_t es, size_t ext, size_t stride, size_t batch, const char *what, std::string *why) {
+    if (ext == 0) return GS_STATUS_SUCCESS;
+    if (stride < ext) {
+        *why = std::string(what) + ": stride smaller than one matrix extent (InvalidStride)";
+        return GS_STATUS_INVALID_VALUE;
+    }
+    const size_t need = ((batch - 1) * stride + ext) * es;
+    if (len < need) {
+        *why = std::string(what) + ": buffer too small (BufferTooSmall)";
+        return GS_STATUS_INVALID_VALUE;
+    }
+    return GS_STATUS_SUCCESS;
+}
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+extern "C" gs_status gs_gemm_strided_batched_ex(gs_handle, int, int, int, int, int, const void *, const void *, int,
+                                                int, long long, const void *, int, int, long long, const void *, void *,
+                                                int, int, long long, int, int, int);
+
+
+extern "C" gs_status gs_host_gemm_ex(gs_handle h, const gs_ex_desc *d) {
+    if (!h) return GS_STATUS_NOT_INITIALIZED;
+    gs::Context &ctx = h->ctx;
+    if (!d) return GS_STATUS_INVALID_VALUE;
+    std::string why;
+    if (d->batch_count == 0) {
+        ctx.last_error = "batch_count == 0 (InvalidBatchCount)";
+        return GS_STATUS_INVALID_VALUE;
+    }
+    if (d->layout != GS_LAYOUT_ROW_MAJOR && d->layout != GS_LAYOUT_COL_MAJOR) {
+        ctx.last_error = "invalid layout";
+        return GS_STATUS_INVALID_VALUE;
+    }
+    const size_t esa = type_size(d->a_type), esb = type_size(d->b_type), esc = type_size(d->c_type);
+    if (!esa || !esb || !esc) {
+        ctx.last_error = "unsupported data type";
+        return GS_STATUS_NOT_SUPPORTED;
+    }
+    const bool ta = d->op_a != GS_OP_N, tb = d->op_b != GS_OP_N;
+    const size_t a_ext = extent(d->layout, d->lda, ta ? d->k : d->m, ta ? d->m : d->k);
+    const size_t b_ext = extent(d->layout, d->ldb, tb ? d->n : d->k, tb ? d->k : d->n);
+    const size_t c_ext = extent(d->layout, d->ldc, d->m, d->n);
+    const size_t sa = d->stride_a ? d->stride_a : a_ext;
+    const size_t sb = d->stride_b ? d->stride_b : b_ext;
+    const size_t sc = d->stride_c ? d->stride_c : c_ext;
+    gs_status st;
+    if ((st = check_len(d->a_len, esa, a_ext, sa, d->batch_count, "a", &why)) != GS_STATUS_SUCCESS ||
+        (st = check_len(d->b_len, esb, b_ext, sb, d->batch_count, "b", &why)) != GS_STATUS_SUCCESS ||
+        (st = check_len(d->c_len, esc, c_ext, sc, d->batch_count, "c", &why)) != GS_STATUS_SUCCESS) {
+        ctx.last_error = why;
+        return st;
+    }
+    if (d->m == 0 || d->n == 0) return GS_STATUS_SUCCESS;
+    const size_t lim = 0x7fffffff;
+    if (d->m > lim || d->n > lim || d->k > lim || d->lda > lim || d->ldb > lim || d->ldc > lim || d->batch_count > lim) {
+        ctx.last_error = "dimension exceeds the 32-bit device API";
+        return GS_STATUS_NOT_SUPPORTED;
+    }
+
+    // alpha / beta in the compute type's host representation.
+    float af = static_cast<float>(d->alpha_re), bf = static_cast<float>(d->beta_re);
+    int32_t ai = 0, bi = 0;
+    uint16_t ah = 0, bh = 0;
+    const void *alpha = &af, *beta = &bf;
+    const bool int_compute = d->compute_type == GS_COMPUTE_32I || d->compute_type == GS_COMPUTE_32I_PEDANTIC;
+    const bool half_compute = d->compute_type == GS_COMPUTE_16F || d->compute_type == GS_COMPUTE_16F_PEDANTIC;
+    if (int_compute) {
+        if (d->alpha_re != std::floor(d->alpha_re) || d->beta_re != std::floor(d->beta_re) ||
+            std::fabs(d->alpha_re) > 2147483647.0 || std::fabs(d->beta_re) > 2147483647.0) {
+            ctx.last_error = "32I compute needs integral alpha/beta";
+            return GS_STATUS_NOT_SUPPORTED;
+        }
+        ai = static_cast<int32_t>(d->alpha_re);
+        bi = static_cast<int32_t>(d->beta_re);
+        alpha = &ai;
+        beta = &bi;
+    } else if (half_compute) {
+        // f32 -> f16 bits, round to nearest even (finite, normal-range values).
+        auto to_half = [](float v) -> uint16_t {
+            uint32_t x;
+            std::memcpy(&x, &v, 4);
+            const uint32_t sign = (x >> 16) & 0x8000u;
+            const int e = static_cast<int>((x >> 23) & 0xffu) - 127 + 15;
+            const uint32_t man = x & 0x7fffffu;
+            if (v == 0.0f) return static_cast<uint16_t>(sign);
+            if (e >= 31) return static_cast<uint16_t>(sign | 0x7c00u);
+            if (e <= 0) return static_cast<uint16_t>(sign);
+            uint32_t val = (static_cast<uint32_t>(e) << 10) | (man >> 13);
+            const uint32_t rem = man & 0x1fffu;
+            if (rem > 0x1000u || (rem == 0x1000u && (val & 1u))) val++;
+            return static_cast<uint16_t>(sign | val);
+        };
+        ah = to_half(af);
+        bh = to_half(bf);
+        alpha = &ah;
+        beta = &bh;
+    }
+
+    // Stage A, B, C in one device region.
+    const size_t a_bytes = ((d->batch_count - 1) * sa + a_ext) * esa;
+    const size_t b_bytes = ((d->batch_count - 1) * sb + b_ext) * esb;
+    const size_t c_bytes = ((d->batch_count - 1) * sc + c_ext) * esc;
+    const size_t off_b = round_up(a_bytes, 256), off_c = off_b + round_up(b_bytes, 256);
+    const size_t need = off_c + round_up(c_bytes, 256);
+    if (ctx.stage_bytes < need) {
+        if (ctx.stage) cudaFree(ctx.stage);
+        ctx.stage = nullptr;
+        ctx.stage_bytes = 0;
+        if (cudaMalloc(&ctx.stage, need) != cudaSuccess) {
+            cudaGetLastError();
+            ctx.last_error = "device staging allocation failed";
+            return GS_STATUS_ALLOC_FAILED;
+        }
+        ctx.stage_bytes = need;
+    }
+    uint8_t *dA = static_cast<uint8_t *>(ctx.stage);
+    uint8_t *dB = dA + off_b;
+    uint8_t *dC = dA + off_c;
+    cudaStream_t s = ctx.stream;
+    // C is uploaded whenever it is read (beta != 0) or has bytes between its
+    // elements that the download must leave untouched.
+    const bool c_dense = (d->layout == GS_LAYOUT_COL_MAJOR ? d->ldc == d->m : d->ldc == d->n) &&
+                         (d->batch_count == 1 || sc == c_ext);
+    const bool upload_c = d->beta_re != 0.0 || !c_dense;
+    cudaError_t e = cudaMemcpyAsync(dA, d->a, a_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dB, d->b, b_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && upload_c) e = cudaMemcpyAsync(dC, d->c, c_bytes, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+        ctx.last_error = std::string("host to device copy: ") + cudaGetErrorString(e);
+        return GS_STATUS_EXECUTION_FAILED;
+    }
+    // Row-major C = op(A) op(B) is column-major C^T = op(B)^T op(A)^T.
+    const bool rm = d->layout == GS_LAYOUT_ROW_MAJOR;
+    const int m = static_cast<int>(rm ? d->n : d->m), n = static_cast<int>(rm ? d->m : d->n);
+    const int opx = rm ? d->op_b : d->op_a, opy = rm ? d->op_a : d->op_b;
+    const void *X = rm ? static_cast<const void *>(dB) : dA;
+    const void *Y = rm ? static_cast<const void *>(dA) : dB;
+    const int ldx = static_cast<int>(rm ? d->ldb : d->lda), ldy = static_cast<int>(rm ? d->lda : d->ldb);
+    const long long sx = static_cast<long long>(rm ? sb : sa), sy = static_cast<long long>(rm ? sa : sb);
+    const int tx = rm ? d->b_type : d->a_type, ty = rm ? d->a_type : d->b_type;
+    st = gs_gemm_strided_batched_ex(h, opx, opy, m, n, static_cast<int>(d->k), alpha, X, tx, ldx, sx, Y, ty, ldy, sy,
+                                    beta, dC, d->c_type, static_cast<int>(d->ldc), static_cast<long long>(sc),
+                                    static_cast<int>(d->batch_count), d->compute_type, d->algo);
+    if (st != GS_STATUS_SUCCESS) return st;
+    e = cudaMemcpyAsync(d->c, dC, c_bytes, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        ctx.last_error = std::string("device to host copy: ") + cudaGetErrorString(e);
+        return GS_STATUS_EXECUTION_FAILED;
+    }
+    return GS_STATUS_SUCCESS;
+}
