@@ -40,7 +40,7 @@ static EncodeTiledFn get_encoder() {
 
 bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t dim0, uint64_t dim1,
                     uint64_t dim2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
-                    std::string *why) {
+                    std::string *why, CUtensorMapSwizzle swizzle) {
     EncodeTiledFn enc = get_encoder();
     if (!enc) {
         if (why) *why = "cuTensorMapEncodeTiled unavailable";
@@ -51,7 +51,7 @@ bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *bas
     cuuint32_t box[3] = {box0, box1, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         if (why) *why = "cuTensorMapEncodeTiled returned " + std::to_string(static_cast<int>(r));
         return false;
@@ -350,8 +350,10 @@ gs_status gs_gemm_strided_batched_ex(gs_handle h, int transa, int transb, int m,
                                      const void *A, int Atype, int lda, long long strideA, const void *B, int Btype,
                                      int ldb, long long strideB, const void *beta, void *C, int Ctype, int ldc,
                                      long long strideC, int batchCount, int computeType, int algo) {
-    (void)algo;  // accepted and ignored, as src/gemm.zig:687 does
+    // algo never changes results (src/gemm.zig:687 ignores it); it is used
+    // only as a tile-shape hint for the tensor-core kernel.
     GemmDesc d{};
+    d.algo = algo;
     gs_status st = check_shape(h, transa, transb, m, n, k, lda, ldb, ldc, batchCount, &d);
     if (st != GS_STATUS_SUCCESS) return st;
     TypedArgs t;
@@ -438,8 +440,8 @@ gs_status gs_gemm_batched_ex(gs_handle h, int transa, int transb, int m, int n, 
                              const void *const Aarray[], int Atype, int lda, const void *const Barray[], int Btype,
                              int ldb, const void *beta, void *const Carray[], int Ctype, int ldc, int batchCount,
                              int computeType, int algo) {
-    (void)algo;
     GemmDesc d{};
+    d.algo = algo;
     gs_status st = check_shape(h, transa, transb, m, n, k, lda, ldb, ldc, batchCount, &d);
     if (st != GS_STATUS_SUCCESS) return st;
     TypedArgs t;

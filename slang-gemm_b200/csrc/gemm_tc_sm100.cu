@@ -8,18 +8,24 @@
 // path of tools/emit_nvcoop2_spv.zig); the arithmetic contract is gemmExCuda
 // (src/gemm.zig:671-706).
 //
-// Design (one CTA per SM, persistent over output tiles):
-//  - tile 128 (M) x 256 (N), 128 bytes of K per pipeline stage, 4 stages;
+// Design (persistent over output tiles, one CTA per SM):
+//  - CG = 2 (default for M > 128): a cluster of two CTAs computes a 256 x 256
+//    tile with tcgen05.mma.cta_group::2. Each CTA loads 128 rows of A and 128
+//    of the 256 B columns, so per-SM operand traffic is 2/3 of the 1-SM tile;
+//    CG = 1: one CTA computes a 128 x 256 tile;
+//  - 128 bytes of K per pipeline stage (64 f16/bf16 or 128 s8), 6 stages (CG 2)
+//    or 4 stages (CG 1);
 //  - warp 0: TMA producer. Operand transposes live in the tensor maps: op(A)=N
 //    (M-contiguous) and op(B)=T (N-contiguous) are fetched as MN-major 128-byte
 //    swizzled panels, op(A)=T and op(B)=N as K-major panels, and the UMMA
 //    instruction descriptor's major bits tell the tensor core which is which;
-//  - warp 1: allocates 512 TMEM columns (two 128x256 accumulators) and issues
-//    tcgen05.mma from one thread; tcgen05.commit frees smem stages and
-//    publishes finished accumulators;
+//  - warp 1: allocates 512 TMEM columns (two 128 x 256 f32/s32 accumulators)
+//    and, in the even CTA only, issues tcgen05.mma from one thread;
+//    tcgen05.commit frees shared-memory stages and publishes accumulators
+//    (to both CTAs of the pair for CG 2);
 //  - warps 2..5: epilogue. tcgen05.ld pulls one accumulator row per thread;
 //    because C is column-major, the 32 lanes of a warp store 32 consecutive
-//    rows of one column (one 128-byte segment per instruction for f32/i32).
+//    rows of one column (one 128-byte segment per instruction for f32/s32).
 //    Double-buffered TMEM lets the epilogue of tile i overlap the main loop of
 //    tile i+1.
 // Batches (strided or pointer-array) are the outermost tile coordinate; the
@@ -34,16 +40,25 @@
 namespace gs {
 namespace tc {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK_BYTES = 128;
-constexpr int STAGES = 4;
-constexpr int A_STAGE_BYTES = BM * BK_BYTES;  // 16 KiB
-constexpr int B_STAGE_BYTES = BN * BK_BYTES;  // 32 KiB
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int BM = 128;        // accumulator rows per CTA
+constexpr int BN = 256;        // accumulator columns per tile
+constexpr int BK_BYTES = 128;  // K bytes per stage
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int NUM_THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*alignment slack*/ + 256 /*barriers*/;
+
+template <int CG>
+struct Cfg {
+    static constexpr int STAGES = CG == 2 ? 6 : 4;
+    static constexpr int B_ROWS = BN / CG;                 // B columns this CTA loads per tile
+    static constexpr int A_STAGE = BM * BK_BYTES;          // 16 KiB
+    static constexpr int B_STAGE = B_ROWS * BK_BYTES;      // 16 KiB (CG 2) / 32 KiB (CG 1)
+    static constexpr int STAGE = A_STAGE + B_STAGE;
+    static constexpr int TILE_M = BM * CG;                 // rows of one (pair) tile
+    // Epilogue staging for TMA stores: per epilogue warp two 32 x 32 x 4-byte blocks.
+    static constexpr int STG_BLOCK = 32 * 32 * 4;
+    static constexpr int STG_BYTES = 4 * 2 * STG_BLOCK;    // 32 KiB
+    static constexpr int SMEM = STAGES * STAGE + STG_BYTES + 1024 /*alignment slack*/ + 256 /*barriers*/;
+};
 
 struct TcArgs {
     int m, n, k, batch;
@@ -58,6 +73,7 @@ struct TcArgs {
     const CUtensorMap *a_maps;   // pointer-array batches: per-batch maps in global memory
     const CUtensorMap *b_maps;
     const uint32_t *skip_flag;   // pointer-array batches: set when a pointer is not 16-byte aligned
+    int tma_store;               // epilogue writes C with TMA tensor stores (beta == 0, C TMA-addressable)
     Epilogue ep;
     uint32_t *err;
 };
@@ -74,9 +90,12 @@ __device__ __forceinline__ void tile_coords(const TcArgs &a, long long t, int &b
     nb = within / gm;
 }
 
-template <int IN, int OUT>
+template <int IN, int OUT, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcArgs args) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmC, const TcArgs args) {
+    using C_ = Cfg<CG>;
+    constexpr int STAGES = C_::STAGES;
     constexpr int ES = (IN == IN_I8) ? 1 : 2;          // element bytes
     constexpr int BK = BK_BYTES / ES;                  // K elements per stage
     constexpr int UK = (IN == IN_I8) ? 32 : 16;        // K per tcgen05.mma
@@ -88,8 +107,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *smA = smem;
-    uint8_t *smB = smem + STAGES * A_STAGE_BYTES;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smB + STAGES * B_STAGE_BYTES);
+    uint8_t *smB = smem + STAGES * C_::A_STAGE;
+    uint8_t *stg = smB + STAGES * C_::B_STAGE;
+    uint64_t *full = reinterpret_cast<uint64_t *>(stg + C_::STG_BYTES);
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;
     uint64_t *tempty = tfull + 2;
@@ -97,9 +117,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;  // position in the CTA pair
+    const bool leader = rank == 0;
 
     // Pointer-array batches whose pointers TMA cannot address are computed by
-    // the CUDA-core kernel launched after this one instead.
+    // the CUDA-core kernel launched after this one instead. Every CTA reads
+    // the same word, so both CTAs of a pair leave together.
     if (args.skip_flag != nullptr && *args.skip_flag != 0u) return;
 
     if (threadIdx.x == 0) {
@@ -109,7 +132,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 128);
+            // CG 1: all 128 epilogue threads arrive; CG 2: one lane per epilogue warp of both CTAs.
+            mbar_init(&tempty[i], CG == 2 ? 8 : 128);
         }
         fence_barrier_init();
     }
@@ -118,24 +142,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         prefetch_tensormap(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_holder, TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (CG == 2) {
+            tmem_alloc_2sm(tmem_holder, TMEM_COLS);
+            tmem_relinquish_2sm();
+        } else {
+            tmem_alloc(tmem_holder, TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();  // the peer's barriers are initialised before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
+    const long long tile0 = CG == 2 ? (blockIdx.x >> 1) : blockIdx.x;
+    const long long tile_step = CG == 2 ? (gridDim.x >> 1) : gridDim.x;
+
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer (both CTAs) ----------------
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (long long t = blockIdx.x; ok && t < args.total_tiles; t += gridDim.x) {
+            for (long long t = tile0; ok && t < args.total_tiles; t += tile_step) {
                 int b, mb, nb;
                 tile_coords(args, t, b, mb, nb);
-                const int m0 = mb * BM, n0 = nb * BN;
+                const int m0 = mb * C_::TILE_M + static_cast<int>(rank) * BM;
+                const int n0 = nb * BN + static_cast<int>(rank) * C_::B_ROWS;
                 const CUtensorMap *ma = &tmA, *mbp = &tmB;
                 int ab = args.a_bcast ? 0 : b, bb = args.b_bcast ? 0 : b;
                 if (args.a_maps != nullptr) {
@@ -148,35 +182,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 for (int kb = 0; kb < args.k_blocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, 1)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                    uint8_t *dA = smA + stage * A_STAGE_BYTES;
-                    uint8_t *dB = smB + stage * B_STAGE_BYTES;
+                    uint8_t *dA = smA + stage * C_::A_STAGE;
+                    uint8_t *dB = smB + stage * C_::B_STAGE;
                     const int k0 = kb * BK;
-                    if (args.a_mn) {
+                    if constexpr (CG == 2) {
+                        // Both CTAs' bytes complete on the even CTA's barrier.
+                        const uint32_t fbar = mapa_shared(smem_u32(&full[stage]), 0);
+                        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C_::STAGE);
+                        if (args.a_mn) {
 #pragma unroll
-                        for (int c = 0; c < BM / CH; ++c) tma_load_3d(dA + c * CH_BYTES, ma, &full[stage], m0 + c * CH, k0, ab);
-                    } else {
-                        tma_load_3d(dA, ma, &full[stage], k0, m0, ab);
-                    }
-                    if (args.b_mn) {
+                            for (int c = 0; c < BM / CH; ++c) tma_load_3d_2sm(dA + c * CH_BYTES, ma, fbar, m0 + c * CH, k0, ab);
+                        } else {
+                            tma_load_3d_2sm(dA, ma, fbar, k0, m0, ab);
+                        }
+                        if (args.b_mn) {
 #pragma unroll
-                        for (int c = 0; c < BN / CH; ++c) tma_load_3d(dB + c * CH_BYTES, mbp, &full[stage], n0 + c * CH, k0, bb);
+                            for (int c = 0; c < C_::B_ROWS / CH; ++c) tma_load_3d_2sm(dB + c * CH_BYTES, mbp, fbar, n0 + c * CH, k0, bb);
+                        } else {
+                            tma_load_3d_2sm(dB, mbp, fbar, k0, n0, bb);
+                        }
                     } else {
-                        tma_load_3d(dB, mbp, &full[stage], k0, n0, bb);
+                        mbar_arrive_expect_tx(&full[stage], C_::STAGE);
+                        if (args.a_mn) {
+#pragma unroll
+                            for (int c = 0; c < BM / CH; ++c) tma_load_3d(dA + c * CH_BYTES, ma, &full[stage], m0 + c * CH, k0, ab);
+                        } else {
+                            tma_load_3d(dA, ma, &full[stage], k0, m0, ab);
+                        }
+                        if (args.b_mn) {
+#pragma unroll
+                            for (int c = 0; c < C_::B_ROWS / CH; ++c) tma_load_3d(dB + c * CH_BYTES, mbp, &full[stage], n0 + c * CH, k0, bb);
+                        } else {
+                            tma_load_3d(dB, mbp, &full[stage], k0, n0, bb);
+                        }
                     }
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            const uint32_t idesc = umma_idesc(C_FMT, AB_FMT, args.a_mn, args.b_mn, BM, BN);
+        // ---------------- MMA issuer (even CTA only) ----------------
+        if (lane == 0 && leader) {
+            const uint32_t idesc = umma_idesc(C_FMT, AB_FMT, args.a_mn, args.b_mn, C_::TILE_M, BN);
             int stage = 0;
             uint32_t phase = 0;
             int it = 0;
             bool ok = true;
-            for (long long t = blockIdx.x; ok && t < args.total_tiles; t += gridDim.x, ++it) {
+            for (long long t = tile0; ok && t < args.total_tiles; t += tile_step, ++it) {
                 const int acc = it & 1;
                 const uint32_t acc_phase = (it >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, 2)) break;
@@ -185,36 +237,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int kb = 0; kb < args.k_blocks; ++kb) {
                     if (!mbar_wait(&full[stage], phase, args.err, 3)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_base = smem_u32(smA + stage * A_STAGE_BYTES);
-                    const uint32_t b_base = smem_u32(smB + stage * B_STAGE_BYTES);
+                    const uint32_t a_base = smem_u32(smA + stage * C_::A_STAGE);
+                    const uint32_t b_base = smem_u32(smB + stage * C_::B_STAGE);
 #pragma unroll
                     for (int kk = 0; kk < BK / UK; ++kk) {
                         const uint64_t adesc = args.a_mn ? umma_smem_desc_sw128(a_base + kk * UK * 128, CH_BYTES, 1024)
                                                          : umma_smem_desc_sw128(a_base + kk * UK * ES, 16, 1024);
                         const uint64_t bdesc = args.b_mn ? umma_smem_desc_sw128(b_base + kk * UK * 128, CH_BYTES, 1024)
                                                          : umma_smem_desc_sw128(b_base + kk * UK * ES, 16, 1024);
-                        if constexpr (IN == IN_I8) umma_i8(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0);
-                        else umma_f16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0);
+                        const uint32_t accum = (kb | kk) != 0;
+                        if constexpr (CG == 2) {
+                            if constexpr (IN == IN_I8) umma_i8_2sm(d_tmem, adesc, bdesc, idesc, accum);
+                            else umma_f16_2sm(d_tmem, adesc, bdesc, idesc, accum);
+                        } else {
+                            if constexpr (IN == IN_I8) umma_i8(d_tmem, adesc, bdesc, idesc, accum);
+                            else umma_f16(d_tmem, adesc, bdesc, idesc, accum);
+                        }
                     }
-                    umma_commit(&empty[stage]);
+                    if constexpr (CG == 2) umma_commit_2sm(&empty[stage], 0x3);
+                    else umma_commit(&empty[stage]);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
-                if (ok) umma_commit(&tfull[acc]);
+                if (ok) {
+                    if constexpr (CG == 2) umma_commit_2sm(&tfull[acc], 0x3);
+                    else umma_commit(&tfull[acc]);
+                }
             }
         }
     } else {
-        // ---------------- epilogue warps 2..5 ----------------
+        // ---------------- epilogue warps 2..5 (both CTAs) ----------------
         const int quad = warp & 3;  // TMEM lane quadrant this warp may access
         const int row = quad * 32 + lane;
+        const uint32_t tempty_leader = CG == 2 ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
+        int stg_flip = 0;
         int it = 0;
-        for (long long t = blockIdx.x; t < args.total_tiles; t += gridDim.x, ++it) {
+        for (long long t = tile0; t < args.total_tiles; t += tile_step, ++it) {
             int b, mb, nb;
             tile_coords(args, t, b, mb, nb);
             const int acc = it & 1;
             const uint32_t acc_phase = (it >> 1) & 1;
             if (!mbar_wait(&tfull[acc], acc_phase, args.err, 4)) break;
             tc_fence_after();
-            const int m = mb * BM + row;
+            const int m = mb * C_::TILE_M + static_cast<int>(rank) * BM + row;
             const int n0 = nb * BN;
             void *Cb = args.C;
             if (args.c_arr != nullptr) Cb = args.c_arr[b];
@@ -226,6 +290,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c, r);
                 tmem_wait_ld();
+                if (args.tma_store) {
+                    // Stage this warp's 32 rows x 32 columns (column-major, like C) and
+                    // write them with one TMA tensor store; edge elements are clipped by TMA.
+                    if (c >= ncols) continue;
+                    uint8_t *buf = stg + ((warp - 2) * 2 + stg_flip) * C_::STG_BLOCK;
+                    stg_flip ^= 1;
+                    if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` has read it
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if constexpr (OUT == OUT_I32) {
+                            int32_t v = static_cast<int32_t>(r[j]);
+                            if (!args.ep.identity) {
+                                double t = __dmul_rn(static_cast<double>(args.ep.alpha_i), static_cast<double>(v));
+                                t = fmin(2147483647.0, fmax(-2147483648.0, round(t)));
+                                v = static_cast<int32_t>(t);
+                            }
+                            reinterpret_cast<int32_t *>(buf)[j * 32 + lane] = v;
+                        } else {
+                            float v = __uint_as_float(r[j]);
+                            if (!args.ep.identity) v = args.ep.alpha_f * v;
+                            if constexpr (OUT == OUT_F32) reinterpret_cast<float *>(buf)[j * 32 + lane] = v;
+                            else if constexpr (OUT == OUT_F16) reinterpret_cast<__half *>(buf)[j * 32 + lane] = __float2half_rn(v);
+                            else reinterpret_cast<uint16_t *>(buf)[j * 32 + lane] = bf16_bits_ref_round(v);
+                        }
+                    }
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_3d(&tmC, buf, mb * C_::TILE_M + static_cast<int>(rank) * BM + quad * 32, n0 + c, b);
+                        bulk_commit_group();
+                    }
+                    continue;
+                }
                 if (m < args.m && c < ncols) {
                     const int jn = min(32, ncols - c);
 #pragma unroll
@@ -239,16 +337,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            if constexpr (CG == 2) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
+            } else {
+                mbar_arrive(&tempty[acc]);
+            }
         }
+        if (args.tma_store && lane == 0) bulk_wait_group_all();  // C is written before the kernel ends
     }
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();  // neither CTA leaves while the peer may still signal its barriers
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        if constexpr (CG == 2) tmem_dealloc_2sm(tmem_base, TMEM_COLS);
+        else tmem_dealloc(tmem_base, TMEM_COLS);
     }
 }
 
@@ -271,41 +377,90 @@ __global__ void k_build_ptr_maps(const CUtensorMap tmpl_a, const CUtensorMap tmp
     maps_a[i] = tmpl_a;
     maps_b[i] = tmpl_b;
     asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;"
-                 ::"l"(reinterpret_cast<uint64_t>(maps_a + i)), "l"(reinterpret_cast<uint64_t>(a_arr[i])) : "memory");
+                 ::"l"(reinterpret_cast<uint64_t>(maps_a + i)), "l"(pa) : "memory");
     asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;"
-                 ::"l"(reinterpret_cast<uint64_t>(maps_b + i)), "l"(reinterpret_cast<uint64_t>(b_arr[i])) : "memory");
+                 ::"l"(reinterpret_cast<uint64_t>(maps_b + i)), "l"(pb) : "memory");
     asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
 }
 
-template <int IN, int OUT>
-static cudaError_t launch_kernel(Context &ctx, const CUtensorMap &ta, const CUtensorMap &tb, const TcArgs &args) {
-    auto kern = k_gemm_tc<IN, OUT>;
+// Largest number of co-resident CTA pairs for the 2-SM kernel on this device.
+template <typename K>
+static int max_pairs(Context &ctx, K kern, int smem) {
+    static int cached[64] = {};
+    if (ctx.device >= 0 && ctx.device < 64 && cached[ctx.device] > 0) return cached[ctx.device];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (ctx.sm_count / 2), 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = ctx.sm_count / 2;
+    }
+    if (ctx.device >= 0 && ctx.device < 64) cached[ctx.device] = n;
+    return n;
+}
+
+template <int IN, int OUT, int CG>
+static cudaError_t launch_kernel(Context &ctx, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tcm,
+                                 const TcArgs &args) {
+    using C_ = Cfg<CG>;
+    auto kern = k_gemm_tc<IN, OUT, CG>;
     static bool attr_set[64] = {};  // per instantiation and device
     cudaError_t e = cudaSuccess;
     if (ctx.device < 0 || ctx.device >= 64 || !attr_set[ctx.device]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM);
         if (e != cudaSuccess) return e;
         if (ctx.device >= 0 && ctx.device < 64) attr_set[ctx.device] = true;
     }
-    const long long grid = args.total_tiles < ctx.sm_count ? args.total_tiles : ctx.sm_count;
-    kern<<<static_cast<unsigned>(grid), NUM_THREADS, SMEM_BYTES, ctx.stream>>>(ta, tb, args);
-    ctx.launches++;
-    return cudaGetLastError();
+    if constexpr (CG == 2) {
+        const long long pairs = args.total_tiles < max_pairs(ctx, kern, C_::SMEM) ? args.total_tiles
+                                                                                 : max_pairs(ctx, kern, C_::SMEM);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = C_::SMEM;
+        cfg.stream = ctx.stream;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, args);
+        ctx.launches++;
+        if (e != cudaSuccess) return e;
+        return cudaGetLastError();
+    } else {
+        const long long grid = args.total_tiles < ctx.sm_count ? args.total_tiles : ctx.sm_count;
+        kern<<<static_cast<unsigned>(grid), NUM_THREADS, C_::SMEM, ctx.stream>>>(ta, tb, tcm, args);
+        ctx.launches++;
+        return cudaGetLastError();
+    }
 }
 
-static cudaError_t dispatch(Context &ctx, const GemmDesc &d, const CUtensorMap &ta, const CUtensorMap &tb,
+template <int CG>
+static cudaError_t dispatch(Context &ctx, const GemmDesc &d, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tcm,
                             const TcArgs &args) {
     switch (d.in_kind) {
     case IN_F16:
-        if (d.out_kind == OUT_F32) return launch_kernel<IN_F16, OUT_F32>(ctx, ta, tb, args);
-        if (d.out_kind == OUT_F16) return launch_kernel<IN_F16, OUT_F16>(ctx, ta, tb, args);
+        if (d.out_kind == OUT_F32) return launch_kernel<IN_F16, OUT_F32, CG>(ctx, ta, tb, tcm, args);
+        if (d.out_kind == OUT_F16) return launch_kernel<IN_F16, OUT_F16, CG>(ctx, ta, tb, tcm, args);
         break;
     case IN_BF16:
-        if (d.out_kind == OUT_F32) return launch_kernel<IN_BF16, OUT_F32>(ctx, ta, tb, args);
-        if (d.out_kind == OUT_BF16) return launch_kernel<IN_BF16, OUT_BF16>(ctx, ta, tb, args);
+        if (d.out_kind == OUT_F32) return launch_kernel<IN_BF16, OUT_F32, CG>(ctx, ta, tb, tcm, args);
+        if (d.out_kind == OUT_BF16) return launch_kernel<IN_BF16, OUT_BF16, CG>(ctx, ta, tb, tcm, args);
         break;
     case IN_I8:
-        if (d.out_kind == OUT_I32) return launch_kernel<IN_I8, OUT_I32>(ctx, ta, tb, args);
+        if (d.out_kind == OUT_I32) return launch_kernel<IN_I8, OUT_I32, CG>(ctx, ta, tb, tcm, args);
         break;
     default: break;
     }
@@ -319,8 +474,9 @@ static CUtensorMapDataType tmap_dtype(InKind k) {
 
 // Encodes the A and B maps. `batch_a`/`batch_b` are the extents of the third
 // (batch) dimension: 1 when every batch entry reads the same matrix.
+// `b_rows` is the number of B columns one CTA loads per tile (256 / CG).
 static bool make_maps(const GemmDesc &d, const void *a_base, const void *b_base, int batch_a, int batch_b,
-                      CUtensorMap *ta, CUtensorMap *tb, std::string *why) {
+                      uint32_t b_rows, CUtensorMap *ta, CUtensorMap *tb, std::string *why) {
     const size_t es = in_elem_size(d.in_kind);
     const uint32_t bk = BK_BYTES / static_cast<uint32_t>(es);
     const uint32_t ch = BK_BYTES / static_cast<uint32_t>(es);
@@ -337,20 +493,39 @@ static bool make_maps(const GemmDesc &d, const void *a_base, const void *b_base,
     const uint64_t b_s1 = static_cast<uint64_t>(d.ldb) * es;
     const uint64_t b_s2 = batch_b > 1 ? static_cast<uint64_t>(d.stride_b) * es : b1 * b_s1;
     if (!encode_tmap_3d(tb, dt, b_base, b0, b1, static_cast<uint64_t>(batch_b), b_s1, b_s2,
-                        d.trans_b ? ch : bk, d.trans_b ? bk : static_cast<uint32_t>(BN), why))
+                        d.trans_b ? ch : bk, d.trans_b ? bk : b_rows, why))
         return false;
     return true;
 }
 
-static TcArgs make_args(Context &ctx, const GemmDesc &d) {
+// Encodes the tensor map the epilogue stores C through (32 x 32 boxes, no
+// swizzle). Only for beta == 0 (C is not read) and a C that TMA can address:
+// 16-byte aligned base, leading dimension and batch stride.
+static bool make_c_map(const GemmDesc &d, CUtensorMap *tcm) {
+    if (!d.ep.beta_zero) return false;
+    const uint64_t es = out_elem_size(d.out_kind);
+    if ((reinterpret_cast<uintptr_t>(d.C) & 15u) != 0 || (static_cast<uint64_t>(d.ldc) * es) % 16 != 0) return false;
+    if (d.batch > 1 && (d.stride_c <= 0 || (static_cast<uint64_t>(d.stride_c) * es) % 16 != 0)) return false;
+    const CUtensorMapDataType dt = d.out_kind == OUT_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : d.out_kind == OUT_I32 ? CU_TENSOR_MAP_DATA_TYPE_INT32
+                                   : d.out_kind == OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const uint64_t s1 = static_cast<uint64_t>(d.ldc) * es;
+    const uint64_t s2 = d.batch > 1 ? static_cast<uint64_t>(d.stride_c) * es : static_cast<uint64_t>(d.n) * s1;
+    return encode_tmap_3d(tcm, dt, d.C, static_cast<uint64_t>(d.m), static_cast<uint64_t>(d.n),
+                          static_cast<uint64_t>(d.batch), s1, s2, 32, 32, nullptr, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+static TcArgs make_args(Context &ctx, const GemmDesc &d, int cg) {
     const int es = static_cast<int>(in_elem_size(d.in_kind));
     const int bk = BK_BYTES / es;
+    const int tile_m = BM * cg;
     TcArgs a{};
     a.m = d.m;
     a.n = d.n;
     a.k = d.k;
     a.batch = d.batch;
-    a.m_blocks = (d.m + BM - 1) / BM;
+    a.m_blocks = (d.m + tile_m - 1) / tile_m;
     a.n_blocks = (d.n + BN - 1) / BN;
     a.k_blocks = (d.k + bk - 1) / bk;
     a.tiles_per_batch = static_cast<long long>(a.m_blocks) * a.n_blocks;
@@ -359,7 +534,8 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d) {
     a.b_mn = d.trans_b ? 1 : 0;
     a.a_bcast = (d.batch == 1 || d.stride_a == 0) ? 1 : 0;
     a.b_bcast = (d.batch == 1 || d.stride_b == 0) ? 1 : 0;
-    a.group_m = a.m_blocks < 16 ? a.m_blocks : 16;
+    const int group = cg == 2 ? 8 : 16;
+    a.group_m = a.m_blocks < group ? a.m_blocks : group;
     a.C = d.C;
     a.ldc = d.ldc;
     a.stride_c = d.stride_c;
@@ -372,24 +548,37 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d) {
     return a;
 }
 
+// CTA-group choice. The algo argument is honoured as a hint (CUBLAS_GEMM_ALGO0
+// = 1-SM 128 x 256 tile, CUBLAS_GEMM_ALGO1 = 2-SM 256 x 256 pair tile); any
+// other value picks the pair tile whenever M > 128 gives both CTAs rows.
+static int choose_cg(const Context &, const GemmDesc &d) {
+    if (d.algo == 0) return 1;
+    if (d.algo == 1) return 2;
+    return d.m > BM ? 2 : 1;
+}
+
 }  // namespace tc
 
 cudaError_t launch_tc(Context &ctx, const GemmDesc &d) {
     using namespace tc;
-    TcArgs args = make_args(ctx, d);
+    const int cg = choose_cg(ctx, d);
+    TcArgs args = make_args(ctx, d, cg);
     CUtensorMap ta, tb;
     std::string why;
-    if (!make_maps(d, d.A, d.B, args.a_bcast ? 1 : d.batch, args.b_bcast ? 1 : d.batch, &ta, &tb, &why)) {
+    if (!make_maps(d, d.A, d.B, args.a_bcast ? 1 : d.batch, args.b_bcast ? 1 : d.batch, BN / cg, &ta, &tb, &why)) {
         ctx.last_error = "tensor map encode failed: " + why;
         return cudaErrorInvalidValue;
     }
-    return dispatch(ctx, d, ta, tb, args);
+    CUtensorMap tcm = ta;  // placeholder when the epilogue stores directly
+    args.tma_store = make_c_map(d, &tcm) ? 1 : 0;
+    return cg == 2 ? dispatch<2>(ctx, d, ta, tb, tcm, args) : dispatch<1>(ctx, d, ta, tb, tcm, args);
 }
 
 cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
                                 void *const *c_arr) {
     using namespace tc;
-    TcArgs args = make_args(ctx, d);
+    const int cg = choose_cg(ctx, d);
+    TcArgs args = make_args(ctx, d, cg);
     // Template maps over a placeholder (16-byte aligned, never dereferenced
     // through the template) with the per-batch geometry; the builder kernel
     // swaps in each batch entry's address.
@@ -405,10 +594,12 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     CUtensorMap ta, tb;
     std::string why;
     const void *placeholder = ctx.tmap_buf;
-    if (!make_maps(d, placeholder, placeholder, 1, 1, &ta, &tb, &why)) {
+    if (!make_maps(d, placeholder, placeholder, 1, 1, BN / cg, &ta, &tb, &why)) {
         ctx.last_error = "tensor map encode failed: " + why;
         return cudaErrorInvalidValue;
     }
+    const CUtensorMap tcm = ta;  // pointer-array C is stored directly (no per-batch C map)
+    args.tma_store = 0;
     CUtensorMap *maps_a = static_cast<CUtensorMap *>(ctx.tmap_buf);
     CUtensorMap *maps_b = maps_a + d.batch;
     uint32_t *misaligned = ctx.dev_err + 1;
@@ -427,7 +618,7 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     args.b_maps = maps_b;
     args.c_arr = c_arr;
     args.skip_flag = misaligned;
-    e = dispatch(ctx, d, ta, tb, args);
+    e = cg == 2 ? dispatch<2>(ctx, d, ta, tb, tcm, args) : dispatch<1>(ctx, d, ta, tb, tcm, args);
     if (e != cudaSuccess) return e;
     // Runs only when the builder raised the flag (it reads the same word).
     return launch_simt_if_flag(ctx, d, a_arr, b_arr, c_arr, misaligned);

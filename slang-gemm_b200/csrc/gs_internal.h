@@ -34,6 +34,7 @@ struct GemmDesc {
     const void *B; long long ldb, stride_b;
     void *C; long long ldc, stride_c;
     Epilogue ep;
+    int algo;                 // cublasGemmAlgo_t hint: 0 = 1-SM tile, 1 = 2-SM pair tile, else automatic
 };
 
 // Kernel selection made by plan_gemm (pure host logic, no device calls).
@@ -76,7 +77,8 @@ cudaError_t launch_simt_if_flag(Context &ctx, const GemmDesc &d, const void *con
 // Tensor-map encoder obtained from the driver at run time.
 bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t dim0,
                     uint64_t dim1, uint64_t dim2, uint64_t stride1_bytes, uint64_t stride2_bytes,
-                    uint32_t box0, uint32_t box1, std::string *why);
+                    uint32_t box0, uint32_t box1, std::string *why,
+                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 size_t in_elem_size(InKind k);
 size_t out_elem_size(OutKind k);

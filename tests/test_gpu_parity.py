@@ -25,7 +25,7 @@ def extent(rows, cols, ld):
 
 
 def run_case(handle, dt, op_a, op_b, m, n, k, alpha=1.0, beta=0.0, ct=None, pad=(0, 0, 0), batch=1,
-             stride_pad=(0, 0, 0), seed=0, expect_kernel=None, bcast_a=False):
+             stride_pad=(0, 0, 0), seed=0, expect_kernel=None, bcast_a=False, algo=gs.GEMM_DEFAULT):
     """Runs one (strided-batched) gemmEx on the GPU and on the oracle; returns the kernel bits used."""
     rng = np.random.default_rng(seed)
     ct = OUT_OF[dt] if ct is None else ct
@@ -43,10 +43,10 @@ def run_case(handle, dt, op_a, op_b, m, n, k, alpha=1.0, beta=0.0, ct=None, pad=
     c = make_c(rng, max(1, sc * batch), ct)
     da, db, dc = to_dev(a), to_dev(b), to_dev(c)
     if batch == 1:
-        handle.gemm_ex(op_a, op_b, m, n, k, alpha, da, dt, lda, db, dt, ldb, beta, dc, ct, ldc, comp)
+        handle.gemm_ex(op_a, op_b, m, n, k, alpha, da, dt, lda, db, dt, ldb, beta, dc, ct, ldc, comp, algo=algo)
     else:
         handle.gemm_strided_batched_ex(op_a, op_b, m, n, k, alpha, da, dt, lda, sa, db, dt, ldb, sb, beta, dc, ct,
-                                       ldc, sc, batch, comp)
+                                       ldc, sc, batch, comp, algo=algo)
     kernels = handle.last_kernels()
     got = to_host(dc)
     ref = c.copy()
@@ -72,22 +72,35 @@ def run_case(handle, dt, op_a, op_b, m, n, k, alpha=1.0, beta=0.0, ct=None, pad=
 
 
 TC = {gs.R_16F: gs.KERNEL_TC_F16, gs.R_16BF: gs.KERNEL_TC_BF16, gs.R_8I: gs.KERNEL_TC_I8}
+# algo hint: 0 = 1-SM 128x256 tile, 1 = 2-SM 256x256 pair tile (results must not depend on it)
+TILES = [0, 1]
 
 
+@pytest.mark.parametrize("algo", TILES)
 @pytest.mark.parametrize("dt", [gs.R_16F, gs.R_16BF, gs.R_8I])
 @pytest.mark.parametrize("op_a,op_b", [(0, 0), (1, 0), (0, 1), (1, 1)])
-def test_tc_exact_tiles(handle, dt, op_a, op_b):
-    run_case(handle, dt, op_a, op_b, 256, 512, 512, seed=1, expect_kernel=TC[dt])
+def test_tc_exact_tiles(handle, dt, op_a, op_b, algo):
+    run_case(handle, dt, op_a, op_b, 512, 512, 512, seed=1, expect_kernel=TC[dt], algo=algo)
 
 
+@pytest.mark.parametrize("algo", TILES)
 @pytest.mark.parametrize("dt", [gs.R_16F, gs.R_16BF, gs.R_8I])
 @pytest.mark.parametrize("op_a,op_b", [(0, 0), (1, 0), (0, 1), (1, 1)])
-def test_tc_ragged_edges_alpha_beta(handle, dt, op_a, op_b):
-    # M, N, K not multiples of the 128 x 256 x (64|128) tile; alpha/beta applied.
+def test_tc_ragged_edges_alpha_beta(handle, dt, op_a, op_b, algo):
+    # M, N, K not multiples of the 256 x 256 x (64|128) tile; alpha/beta applied.
     q = 16 if dt == gs.R_8I else 8
-    m, n, k = 13 * q + (0 if op_a else 0), 37 * q, 11 * q
+    m, n, k = 41 * q, 37 * q, 11 * q
     alpha, beta = (2.0, -1.0) if dt == gs.R_8I else (1.5, 0.5)
-    run_case(handle, dt, op_a, op_b, m, n, k, alpha=alpha, beta=beta, seed=2, expect_kernel=TC[dt])
+    run_case(handle, dt, op_a, op_b, m, n, k, alpha=alpha, beta=beta, seed=2, expect_kernel=TC[dt], algo=algo)
+
+
+@pytest.mark.parametrize("dt", [gs.R_16F, gs.R_8I])
+def test_tc_small_m_and_single_tile(handle, dt):
+    # M <= 128 picks the 1-SM tile automatically; M = 136 leaves the odd CTA 8 rows.
+    q = 16 if dt == gs.R_8I else 8
+    run_case(handle, dt, 0, 0, 64, 256, 128, seed=3, expect_kernel=TC[dt])
+    run_case(handle, dt, 1, 0, 17 * q, 2 * q, 3 * q, seed=3, expect_kernel=TC[dt], algo=1)
+    run_case(handle, dt, 0, 1, 128, 1024, 4 * q, seed=3, expect_kernel=TC[dt], algo=1)
 
 
 @pytest.mark.parametrize("dt", [gs.R_16F, gs.R_8I])
@@ -110,13 +123,14 @@ def test_unaligned_shapes_use_cuda_core_kernel(handle, dt, op_a, op_b):
         assert kern & gs.KERNEL_SIMT
 
 
+@pytest.mark.parametrize("algo", TILES)
 @pytest.mark.parametrize("dt", [gs.R_16F, gs.R_16BF, gs.R_8I])
-def test_strided_batched(handle, dt):
+def test_strided_batched(handle, dt, algo):
     q = 16 if dt == gs.R_8I else 8
-    run_case(handle, dt, 0, 0, 128, 256, 192, batch=5, seed=6, expect_kernel=TC[dt])
+    run_case(handle, dt, 0, 0, 256, 256, 192, batch=5, seed=6, expect_kernel=TC[dt], algo=algo)
     run_case(handle, dt, 1, 0, 96, 136, 64, batch=3, stride_pad=(q, 2 * q, 7), alpha=2.0 if dt == gs.R_8I else 0.5,
-             beta=1.0 if dt == gs.R_8I else 0.25, seed=7, expect_kernel=TC[dt])
-    run_case(handle, dt, 0, 1, 128, 128, 128, batch=4, bcast_a=True, seed=8, expect_kernel=TC[dt])
+             beta=1.0 if dt == gs.R_8I else 0.25, seed=7, expect_kernel=TC[dt], algo=algo)
+    run_case(handle, dt, 0, 1, 384, 128, 128, batch=4, bcast_a=True, seed=8, expect_kernel=TC[dt], algo=algo)
 
 
 def test_strided_batched_config4_shape_small_batch(handle):
@@ -240,7 +254,8 @@ def test_sgemm_strided_batched(handle):
 
 @pytest.mark.parametrize("dt", [gs.R_16F, gs.R_16BF, gs.R_8I, gs.R_32F])
 @pytest.mark.parametrize("misalign", [False, True])
-def test_pointer_array_batched(handle, dt, misalign):
+@pytest.mark.parametrize("algo", TILES)
+def test_pointer_array_batched(handle, dt, misalign, algo):
     import torch
 
     rng = np.random.default_rng(30 + dt)
@@ -258,7 +273,8 @@ def test_pointer_array_batched(handle, dt, misalign):
     bptr = torch.tensor([t.data_ptr() for t in db], dtype=torch.int64, device="cuda")
     cptr = torch.tensor([t.data_ptr() for t in dc], dtype=torch.int64, device="cuda")
     alpha, beta = (2.0, -1.0) if dt == gs.R_8I else (0.75, 0.5)
-    handle.gemm_batched_ex(0, 0, m, n, k, alpha, aptr, dt, m, bptr, dt, k, beta, cptr, ct, m, batch, COMPUTE[dt])
+    handle.gemm_batched_ex(0, 0, m, n, k, alpha, aptr, dt, m, bptr, dt, k, beta, cptr, ct, m, batch, COMPUTE[dt],
+                           algo=algo)
     kern = handle.last_kernels()
     refs = [x.copy() for x in c_list]
     a_view = [x[shift:shift + m * k].copy() for x in a_list]
@@ -324,3 +340,18 @@ def test_stream_is_honoured(handle):
             run_case(handle, gs.R_16F, 0, 0, 128, 256, 128, seed=50, expect_kernel=gs.KERNEL_TC_F16)
     finally:
         handle.set_stream(None)
+
+
+# ---- TMA-store epilogue (beta == 0, C 16-byte addressable) ------------------
+
+@pytest.mark.parametrize("algo", TILES)
+@pytest.mark.parametrize("dt,ct", [(gs.R_16F, gs.R_32F), (gs.R_16F, gs.R_16F), (gs.R_16BF, gs.R_16BF),
+                                   (gs.R_16BF, gs.R_32F), (gs.R_8I, gs.R_32I)])
+def test_tma_store_epilogue_ragged(handle, dt, ct, algo):
+    # beta = 0 with a TMA-addressable C routes the epilogue through TMA tensor
+    # stores; ragged M / N exercise the clipping of partial 32 x 32 boxes.
+    q = 16 if dt == gs.R_8I else 8
+    alpha = 3.0 if dt == gs.R_8I else 0.75
+    run_case(handle, dt, 0, 0, 37 * q, 45 * q, 9 * q, alpha=alpha, ct=ct, seed=60, expect_kernel=TC[dt], algo=algo)
+    run_case(handle, dt, 1, 1, 19 * q, 13 * q, 5 * q, alpha=1.0, ct=ct, batch=3, stride_pad=(q, q, 8), seed=61,
+             expect_kernel=TC[dt], algo=algo)
