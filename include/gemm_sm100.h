@@ -168,6 +168,30 @@ gs_status gs_plan_gemm_strided_batched_ex(int transa, int transb, int m, int n, 
                                           long long strideB, const void *C, int Ctype, int ldc, long long strideC,
                                           int batchCount, int computeType, uint32_t *kernel);
 
+/* Largest batchCount gs_gemm_batched_ex_noalloc accepts. */
+#define GS_NOALLOC_MAX_BATCH 256
+
+/* Pointer-array batched typed GEMM that allocates no memory and needs no
+ * handle. No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory -- a framework whose caching allocator owns the GPU's
+ * memory, a service with a fixed, pre-planned memory budget, or a
+ * latency-critical path that must not pay the device-wide synchronisation
+ * cudaMalloc/cudaFree can imply. Same arguments, types, semantics and status
+ * codes as gs_gemm_batched_ex, plus the stream (a cudaStream_t) to run on.
+ * Its scratch (per-batch tensor maps and two status words, about 64 KiB) is a
+ * static device array in the library that every GPU loading the library holds
+ * until the process exits. Limit: batchCount <= GS_NOALLOC_MAX_BATCH;
+ * larger batches return GS_STATUS_INVALID_VALUE and launch nothing.
+ * The first call on a device resolves the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture. All calls share the array and each clears the
+ * words that must start at zero, so calls that overlap on the GPU (other
+ * streams or host threads) race: order them on one stream. */
+gs_status gs_gemm_batched_ex_noalloc(void *stream, int transa, int transb, int m, int n, int k, const void *alpha,
+                                     const void *const Aarray[], int Atype, int lda, const void *const Barray[],
+                                     int Btype, int ldb, const void *beta, void *const Carray[], int Ctype, int ldc,
+                                     int batchCount, int computeType);
+
 /* ---------------------------------------------------------------------- */
 /* Host-buffer mirror of gemm.gemmEx                                       */
 /* ---------------------------------------------------------------------- */

@@ -200,12 +200,7 @@ gs_status gs_device_error(gs_handle h, uint32_t *word);
 
 // ---- argument decoding shared by the typed entry points ----------------
 
-namespace {
-
-struct TypedArgs {
-    InKind in;
-    OutKind out;
-};
+namespace gs {
 
 // Maps (Atype, Btype, Ctype, computeType) onto a kernel family, or
 // GS_STATUS_NOT_SUPPORTED (cf. the cuBLAS-supported set the reference bench
@@ -333,7 +328,7 @@ gs_status run(gs_handle h, GemmDesc &d) {
     return from_cuda(h, e, "kernel launch");
 }
 
-}  // namespace
+}  // namespace gs
 
 extern "C" {
 

@@ -83,6 +83,16 @@ bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *bas
 size_t in_elem_size(InKind k);
 size_t out_elem_size(OutKind k);
 
+// Argument decoding shared by the C entry points (capi.cu).
+struct TypedArgs {
+    InKind in;
+    OutKind out;
+};
+gs_status decode_types(int at, int bt, int ct, int comp, TypedArgs *t);
+void read_scalars(int comp, const void *alpha, const void *beta, Epilogue *ep);
+gs_status check_shape_core(int transa, int transb, int m, int n, int k, int lda, int ldb, int ldc, int batch,
+                           GemmDesc *d, std::string *why);
+
 }  // namespace gs
 
 // The object behind gs_handle.

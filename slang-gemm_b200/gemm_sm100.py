@@ -50,6 +50,7 @@ KERNEL_SCALE = 1 << 5
 KERNEL_TMAP = 1 << 6
 
 ELEM_SIZE = {R_32F: 4, R_64F: 8, R_16F: 2, R_8I: 1, R_32I: 4, R_16BF: 2}
+NOALLOC_MAX_BATCH = 256  # GS_NOALLOC_MAX_BATCH
 
 
 class GemmError(RuntimeError):
@@ -108,6 +109,7 @@ def _load() -> ctypes.CDLL:
                                                  ctypes.POINTER(u32)]),
         "gs_host_gemm_ex": (st, [vp, ctypes.POINTER(ExDesc)]),
         "gs_plan_shards": (st, [ll, i, ll, ctypes.POINTER(ll)]),
+        "gs_gemm_batched_ex_noalloc": (st, [vp, i, i, i, i, i, vp, vp, i, i, vp, i, i, vp, vp, i, i, i, i]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -171,6 +173,18 @@ def _scalar(compute: int, v):
 
         return ctypes.c_uint16(int(np.array(v, dtype=np.float16).view(np.uint16)))
     return ctypes.c_float(float(v))
+
+
+def gemm_batched_ex_noalloc(stream, transa, transb, m, n, k, alpha, Aarr, atype, lda, Barr, btype, ldb, beta, Carr,
+                            ctype, ldc, batch, compute) -> int:
+    """gs_gemm_batched_ex_noalloc: pointer-array batched GEMM that allocates no device memory and needs no
+    handle (for callers whose device memory is owned elsewhere). Returns the gs_status; batch is limited to
+    NOALLOC_MAX_BATCH. `stream` is a torch.cuda.Stream, a raw cudaStream_t int, or None."""
+    a, b = _scalar(compute, alpha), _scalar(compute, beta)
+    ptr = getattr(stream, "cuda_stream", stream)
+    return _lib.gs_gemm_batched_ex_noalloc(ptr, transa, transb, m, n, k, ctypes.byref(a), _ptr(Aarr), atype, lda,
+                                           _ptr(Barr), btype, ldb, ctypes.byref(b), _ptr(Carr), ctype, ldc, batch,
+                                           compute)
 
 
 @dataclass
