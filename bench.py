@@ -216,6 +216,16 @@ def max_over_ranks(dist, value: float) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(dist, value: float) -> float:
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def barrier(dist):
     import torch
 
@@ -226,22 +236,21 @@ def barrier(dist):
 
 # ---- our implementation ----------------------------------------------------------
 
-def rank_share(cfg: dict, rank: int, world: int, scaling: str) -> dict:
-    """This rank's share: weak scaling keeps one configuration's worth of work per rank."""
-    import gemm_sm100 as gs
+def rank_share(cfg: dict, rank: int, world: int, scaling: str):
+    """This rank's share and its Shard: weak scaling keeps one configuration's worth of work per
+    rank (the global problem grows with the world), strong scaling splits one configuration."""
+    import sharding
 
     c = dict(cfg)
-    if world == 1:
-        return c
     if cfg["shard"] == "batch":
         total = cfg["batch"] * (world if scaling == "weak" else 1)
-        cuts = gs.plan_shards(total, world, 1)
-        c["batch"] = cuts[rank + 1] - cuts[rank]
+        s = sharding.plan(total, world, rank, "batch", 1)
+        c["batch"] = s.size
     else:
         total = cfg["n"] * (world if scaling == "weak" else 1)
-        cuts = gs.plan_shards(total, world, 256)
-        c["n"] = cuts[rank + 1] - cuts[rank]
-    return c
+        s = sharding.plan(total, world, rank, "cols", 256)
+        c["n"] = s.size
+    return c, s
 
 
 def make_inputs(cfg: dict, seed: int):
@@ -308,7 +317,7 @@ def run_ours(args, cfg_name: str) -> None:
 
     cfg0 = CONFIGS[cfg_name]
     rank, world, local, dist = dist_setup(args.gpus)
-    cfg = rank_share(cfg0, rank, world, args.scaling)
+    cfg, shard = rank_share(cfg0, rank, world, args.scaling)
     peaks = load_peaks()
     stream = torch.cuda.current_stream()
     h = gs.Handle(stream=stream)
@@ -356,7 +365,7 @@ def run_ours(args, cfg_name: str) -> None:
     max_elapsed = max_over_ranks(dist, elapsed)
     max_kernel_ms = max_over_ranks(dist, kernel_ms)
     flops_rank, bytes_rank = work(cfg)
-    total_flops = flops_rank * world if dist is None else max_over_ranks(dist, 0.0) * 0 + flops_rank * world
+    total_flops = sum_over_ranks(dist, flops_rank)
     ms_per_step = max_elapsed / max(1, args.steps)
     value = total_flops / (ms_per_step * 1e-3) / 1e12
 
@@ -413,6 +422,22 @@ def run_ours(args, cfg_name: str) -> None:
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg0, budget_s=args.cpu_seconds)
+    if args.gather and dist is not None:
+        # Optional NCCL all-gather of the C blocks onto every rank, timed on its own
+        # (not part of `value`: the sharded GEMM itself needs no collective).
+        import sharding
+
+        unit = cfg["m"] if cfg0["shard"] == "cols" else cfg["m"] * cfg["n"]
+        sharding.gather_blocks(C, shard, unit)  # warm the communicator
+        barrier(dist)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        full = sharding.gather_blocks(C, shard, unit)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        line["allgather"] = {"ms": round(max_over_ranks(dist, g0.elapsed_time(g1)), 3),
+                             "bytes_per_rank": int(full.numel() * full.element_size()), "backend": "nccl"}
+        del full
     if args.cublas and rank == 0:
         line["cublas"] = cublas_compare(cfg, A, B, args.steps, args.warmup)
     h.close()
@@ -565,6 +590,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--cublas", action="store_true", help="also time cuBLAS (torch.mm) on the same operands")
+    ap.add_argument("--gather", action="store_true", help="N > 1: also time an NCCL all-gather of C (separately)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the cpu_baseline sample")
     ap.add_argument("--ref-seconds", type=float, default=90.0, help="target total length of --impl reference")
