@@ -444,7 +444,7 @@ def run_ours(args, cfg_name: str) -> None:
     if dist is not None:
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def cublas_compare(cfg: dict, A, B, steps: int, warmup: int) -> dict:
@@ -578,10 +578,29 @@ def run_reference(args, cfg_name: str) -> None:
         "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+# The result line is the only thing written to stdout: libraries that print
+# banners (NCCL, for one) see stderr as their stdout while bench.py runs.
+_RESULT_FD = None
+
+
+def emit(line: dict) -> None:
+    data = (json.dumps(line) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, data)
 
 
 def main():
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)

@@ -23,11 +23,13 @@
 //    and, in the even CTA only, issues tcgen05.mma from one thread;
 //    tcgen05.commit frees shared-memory stages and publishes accumulators
 //    (to both CTAs of the pair for CG 2);
-//  - warps 2..5: epilogue. tcgen05.ld pulls one accumulator row per thread;
-//    because C is column-major, the 32 lanes of a warp store 32 consecutive
-//    rows of one column (one 128-byte segment per instruction for f32/s32).
-//    Double-buffered TMEM lets the epilogue of tile i overlap the main loop of
-//    tile i+1.
+//  - warps 2..9: epilogue, two warps per TMEM lane quadrant, each draining
+//    half of the 256 accumulator columns. tcgen05.ld gives each thread one
+//    accumulator row; with beta == 0 a warp stages 32 rows x 16 columns in
+//    shared memory (column-major, like C) and writes them with a TMA tensor
+//    store (L2 evict_first); otherwise the 32 lanes store 32 consecutive rows
+//    of one column directly. Double-buffered TMEM lets the epilogue of tile i
+//    overlap the main loop of tile i+1.
 // Batches (strided or pointer-array) are the outermost tile coordinate; the
 // M/N tiles of one batch are visited in groups of `group_m` row blocks so
 // that concurrently running CTAs share A and B panels in L2.
@@ -44,7 +46,13 @@ constexpr int BM = 128;        // accumulator rows per CTA
 constexpr int BN = 256;        // accumulator columns per tile
 constexpr int BK_BYTES = 128;  // K bytes per stage
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int NUM_THREADS = 192;
+// Epilogue warps: two per TMEM lane quadrant, each draining half of the columns.
+constexpr int EPI_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+// Result stores are streamed through L2 (evict_first) so the output does not
+// push operand panels out; operand loads of a single GEMM are kept
+// (evict_last: its A and B panels are re-read by many tiles), those of batched
+// calls use the normal policy (each batch entry's panels are short-lived).
 
 template <int CG>
 struct Cfg {
@@ -54,9 +62,9 @@ struct Cfg {
     static constexpr int B_STAGE = B_ROWS * BK_BYTES;      // 16 KiB (CG 2) / 32 KiB (CG 1)
     static constexpr int STAGE = A_STAGE + B_STAGE;
     static constexpr int TILE_M = BM * CG;                 // rows of one (pair) tile
-    // Epilogue staging for TMA stores: per epilogue warp two 32 x 32 x 4-byte blocks.
-    static constexpr int STG_BLOCK = 32 * 32 * 4;
-    static constexpr int STG_BYTES = 4 * 2 * STG_BLOCK;    // 32 KiB
+    // Epilogue staging for TMA stores: per epilogue warp two 32-row x 16-column x 4-byte blocks.
+    static constexpr int STG_BLOCK = 32 * 16 * 4;
+    static constexpr int STG_BYTES = EPI_WARPS * 2 * STG_BLOCK;  // 32 KiB
     static constexpr int SMEM = STAGES * STAGE + STG_BYTES + 1024 /*alignment slack*/ + 256 /*barriers*/;
 };
 
@@ -74,6 +82,7 @@ struct TcArgs {
     const CUtensorMap *b_maps;
     const uint32_t *skip_flag;   // pointer-array batches: set when a pointer is not 16-byte aligned
     int tma_store;               // epilogue writes C with TMA tensor stores (beta == 0, C TMA-addressable)
+    int ab_evict_last;           // operand loads use the evict_last L2 policy
     Epilogue ep;
     uint32_t *err;
 };
@@ -132,8 +141,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
-            // CG 1: all 128 epilogue threads arrive; CG 2: one lane per epilogue warp of both CTAs.
-            mbar_init(&tempty[i], CG == 2 ? 8 : 128);
+            // One elected lane per epilogue warp (of both CTAs for CG 2).
+            mbar_init(&tempty[i], CG * EPI_WARPS);
         }
         fence_barrier_init();
     }
@@ -162,6 +171,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
         if (lane == 0) {
+            const uint64_t pol_ab = args.ab_evict_last ? l2_policy_evict_last() : l2_policy_evict_normal();
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -191,29 +201,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C_::STAGE);
                         if (args.a_mn) {
 #pragma unroll
-                            for (int c = 0; c < BM / CH; ++c) tma_load_3d_2sm(dA + c * CH_BYTES, ma, fbar, m0 + c * CH, k0, ab);
+                            for (int c = 0; c < BM / CH; ++c)
+                                tma_load_3d_2sm(dA + c * CH_BYTES, ma, fbar, m0 + c * CH, k0, ab, pol_ab);
                         } else {
-                            tma_load_3d_2sm(dA, ma, fbar, k0, m0, ab);
+                            tma_load_3d_2sm(dA, ma, fbar, k0, m0, ab, pol_ab);
                         }
                         if (args.b_mn) {
 #pragma unroll
-                            for (int c = 0; c < C_::B_ROWS / CH; ++c) tma_load_3d_2sm(dB + c * CH_BYTES, mbp, fbar, n0 + c * CH, k0, bb);
+                            for (int c = 0; c < C_::B_ROWS / CH; ++c)
+                                tma_load_3d_2sm(dB + c * CH_BYTES, mbp, fbar, n0 + c * CH, k0, bb, pol_ab);
                         } else {
-                            tma_load_3d_2sm(dB, mbp, fbar, k0, n0, bb);
+                            tma_load_3d_2sm(dB, mbp, fbar, k0, n0, bb, pol_ab);
                         }
                     } else {
                         mbar_arrive_expect_tx(&full[stage], C_::STAGE);
                         if (args.a_mn) {
 #pragma unroll
-                            for (int c = 0; c < BM / CH; ++c) tma_load_3d(dA + c * CH_BYTES, ma, &full[stage], m0 + c * CH, k0, ab);
+                            for (int c = 0; c < BM / CH; ++c)
+                                tma_load_3d_hint(dA + c * CH_BYTES, ma, &full[stage], m0 + c * CH, k0, ab, pol_ab);
                         } else {
-                            tma_load_3d(dA, ma, &full[stage], k0, m0, ab);
+                            tma_load_3d_hint(dA, ma, &full[stage], k0, m0, ab, pol_ab);
                         }
                         if (args.b_mn) {
 #pragma unroll
-                            for (int c = 0; c < C_::B_ROWS / CH; ++c) tma_load_3d(dB + c * CH_BYTES, mbp, &full[stage], n0 + c * CH, k0, bb);
+                            for (int c = 0; c < C_::B_ROWS / CH; ++c)
+                                tma_load_3d_hint(dB + c * CH_BYTES, mbp, &full[stage], n0 + c * CH, k0, bb, pol_ab);
                         } else {
-                            tma_load_3d(dB, mbp, &full[stage], k0, n0, bb);
+                            tma_load_3d_hint(dB, mbp, &full[stage], k0, n0, bb, pol_ab);
                         }
                     }
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -265,10 +279,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
         }
     } else {
-        // ---------------- epilogue warps 2..5 (both CTAs) ----------------
-        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        // ---------------- epilogue warps 2..2+EPI_WARPS-1 (both CTAs) ----------------
+        const int quad = warp & 3;               // TMEM lane quadrant this warp may access
+        const int ew = warp - 2;                 // epilogue warp index
+        const int c_lo = (ew / 4) * (BN / 2);    // this warp's half of the accumulator columns
         const int row = quad * 32 + lane;
         const uint32_t tempty_leader = CG == 2 ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
+        const uint64_t pol_c = l2_policy_evict_first();
         int stg_flip = 0;
         int it = 0;
         for (long long t = tile0; t < args.total_tiles; t += tile_step, ++it) {
@@ -286,41 +303,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                                         ((OUT == OUT_F16 || OUT == OUT_BF16) ? 2 : 4);
             const int ncols = min(BN, args.n - n0);
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c, r);
                 tmem_wait_ld();
                 if (args.tma_store) {
-                    // Stage this warp's 32 rows x 32 columns (column-major, like C) and
-                    // write them with one TMA tensor store; edge elements are clipped by TMA.
-                    if (c >= ncols) continue;
-                    uint8_t *buf = stg + ((warp - 2) * 2 + stg_flip) * C_::STG_BLOCK;
-                    stg_flip ^= 1;
-                    if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` has read it
-                    __syncwarp();
+                    // Stage this warp's 32 rows in blocks of 16 columns (column-major, like C)
+                    // and write each block with one TMA tensor store; edge elements are
+                    // clipped by TMA. Two staging buffers per warp alternate.
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        if constexpr (OUT == OUT_I32) {
-                            int32_t v = static_cast<int32_t>(r[j]);
-                            if (!args.ep.identity) {
-                                double t = __dmul_rn(static_cast<double>(args.ep.alpha_i), static_cast<double>(v));
-                                t = fmin(2147483647.0, fmax(-2147483648.0, round(t)));
-                                v = static_cast<int32_t>(t);
+                    for (int h = 0; h < 2; ++h) {
+                        if (c + 16 * h >= ncols) continue;
+                        uint8_t *buf = stg + (ew * 2 + stg_flip) * C_::STG_BLOCK;
+                        stg_flip ^= 1;
+                        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` has read it
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const uint32_t raw = r[16 * h + j];
+                            if constexpr (OUT == OUT_I32) {
+                                int32_t v = static_cast<int32_t>(raw);
+                                if (!args.ep.identity) {
+                                    double t = __dmul_rn(static_cast<double>(args.ep.alpha_i), static_cast<double>(v));
+                                    t = fmin(2147483647.0, fmax(-2147483648.0, round(t)));
+                                    v = static_cast<int32_t>(t);
+                                }
+                                reinterpret_cast<int32_t *>(buf)[j * 32 + lane] = v;
+                            } else {
+                                float v = __uint_as_float(raw);
+                                if (!args.ep.identity) v = args.ep.alpha_f * v;
+                                if constexpr (OUT == OUT_F32) reinterpret_cast<float *>(buf)[j * 32 + lane] = v;
+                                else if constexpr (OUT == OUT_F16) reinterpret_cast<__half *>(buf)[j * 32 + lane] = __float2half_rn(v);
+                                else reinterpret_cast<uint16_t *>(buf)[j * 32 + lane] = bf16_bits_ref_round(v);
                             }
-                            reinterpret_cast<int32_t *>(buf)[j * 32 + lane] = v;
-                        } else {
-                            float v = __uint_as_float(r[j]);
-                            if (!args.ep.identity) v = args.ep.alpha_f * v;
-                            if constexpr (OUT == OUT_F32) reinterpret_cast<float *>(buf)[j * 32 + lane] = v;
-                            else if constexpr (OUT == OUT_F16) reinterpret_cast<__half *>(buf)[j * 32 + lane] = __float2half_rn(v);
-                            else reinterpret_cast<uint16_t *>(buf)[j * 32 + lane] = bf16_bits_ref_round(v);
                         }
-                    }
-                    fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_3d(&tmC, buf, mb * C_::TILE_M + static_cast<int>(rank) * BM + quad * 32, n0 + c, b);
-                        bulk_commit_group();
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_3d(&tmC, buf, mb * C_::TILE_M + static_cast<int>(rank) * BM + quad * 32,
+                                         n0 + c + 16 * h, b, pol_c);
+                            bulk_commit_group();
+                        }
                     }
                     continue;
                 }
@@ -337,11 +360,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
             tc_fence_before();
-            if constexpr (CG == 2) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
-            } else {
-                mbar_arrive(&tempty[acc]);
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (CG == 2) mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
+                else mbar_arrive(&tempty[acc]);
             }
         }
         if (args.tma_store && lane == 0) bulk_wait_group_all();  // C is written before the kernel ends
@@ -513,7 +535,7 @@ static bool make_c_map(const GemmDesc &d, CUtensorMap *tcm) {
     const uint64_t s1 = static_cast<uint64_t>(d.ldc) * es;
     const uint64_t s2 = d.batch > 1 ? static_cast<uint64_t>(d.stride_c) * es : static_cast<uint64_t>(d.n) * s1;
     return encode_tmap_3d(tcm, dt, d.C, static_cast<uint64_t>(d.m), static_cast<uint64_t>(d.n),
-                          static_cast<uint64_t>(d.batch), s1, s2, 32, 32, nullptr, CU_TENSOR_MAP_SWIZZLE_NONE);
+                          static_cast<uint64_t>(d.batch), s1, s2, 32, 16, nullptr, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 static TcArgs make_args(Context &ctx, const GemmDesc &d, int cg) {
@@ -543,6 +565,7 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int cg) {
     a.a_maps = nullptr;
     a.b_maps = nullptr;
     a.skip_flag = nullptr;
+    a.ab_evict_last = d.batch == 1 ? 1 : 0;
     a.ep = d.ep;
     a.err = ctx.dev_err;
     return a;

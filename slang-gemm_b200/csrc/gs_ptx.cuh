@@ -81,13 +81,41 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
-// 3-D tiled TMA store shared -> global (bulk-group completion). Elements of
-// the box outside the tensor are not written.
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *smem_src, int32_t c0, int32_t c1,
-                                             int32_t c2) {
+// L2 cache policies for the operand loads (kept) and the result stores (streamed).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// TMA load as tma_load_3d with an L2 cache policy.
+__device__ __forceinline__ void tma_load_3d_hint(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int32_t c0,
+                                                 int32_t c1, int32_t c2, uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
-        ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5}], [%2], %6;"
+        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)),
+          "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+        : "memory");
+}
+
+// 3-D tiled TMA store shared -> global (bulk-group completion) with an L2
+// cache policy. Elements of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *smem_src, int32_t c0, int32_t c1,
+                                             int32_t c2, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%2, %3, %4}], [%1], %5;"
+        ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
         : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -205,14 +233,14 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 }
 
 // 2-SM TMA load: writes this CTA's shared memory, completes on an mbarrier
-// that may be in the peer CTA of the pair (no multicast).
+// that may be in the peer CTA of the pair (no multicast); L2 cache policy.
 __device__ __forceinline__ void tma_load_3d_2sm(void *smem_dst, const CUtensorMap *map, uint32_t mbar_cluster_addr,
-                                                int32_t c0, int32_t c1, int32_t c2) {
+                                                int32_t c0, int32_t c1, int32_t c2, uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5}], [%2];"
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5}], [%2], %6;"
         ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(mbar_cluster_addr),
-          "r"(c0), "r"(c1), "r"(c2)
+          "r"(c0), "r"(c1), "r"(c2), "l"(policy)
         : "memory");
 }
 
