@@ -159,6 +159,14 @@ gs_status gs_destroy(gs_handle h) {
     if (h->ctx.dev_err) cudaFree(h->ctx.dev_err);
     if (h->ctx.stage) cudaFree(h->ctx.stage);
     if (h->ctx.tmap_buf) cudaFree(h->ctx.tmap_buf);
+    if (h->ctx.h2d) cudaStreamDestroy(h->ctx.h2d);
+    if (h->ctx.d2h) cudaStreamDestroy(h->ctx.d2h);
+    if (h->ctx.ev_start) cudaEventDestroy(h->ctx.ev_start);
+    if (h->ctx.ev_a) cudaEventDestroy(h->ctx.ev_a);
+    for (int i = 0; i < Context::kMaxChunks; ++i) {
+        if (h->ctx.ev_in[i]) cudaEventDestroy(h->ctx.ev_in[i]);
+        if (h->ctx.ev_out[i]) cudaEventDestroy(h->ctx.ev_out[i]);
+    }
     if (prev >= 0) cudaSetDevice(prev);
     delete h;
     return GS_STATUS_SUCCESS;
@@ -224,7 +232,8 @@ gs_status decode_types(int at, int bt, int ct, int comp, TypedArgs *t) {
         return GS_STATUS_NOT_SUPPORTED;
     }
     if (at == GS_R_32F) {
-        if (c32f && ct == GS_R_32F) { *t = {IN_F32, OUT_F32}; return GS_STATUS_SUCCESS; }
+        // FAST_TF32 permits, and does not require, TF32 products: it runs the exact-f32 FFMA kernel.
+        if ((c32f || comp == GS_COMPUTE_32F_FAST_TF32) && ct == GS_R_32F) { *t = {IN_F32, OUT_F32}; return GS_STATUS_SUCCESS; }
         return GS_STATUS_NOT_SUPPORTED;
     }
     return GS_STATUS_NOT_SUPPORTED;

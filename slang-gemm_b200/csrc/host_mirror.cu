@@ -4,6 +4,7 @@
 // lengths, row- or column-major layout, stride 0 = one matrix extent),
 // validates them like validateByteSliceLen (src/gemm.zig:769-775), stages the
 // operands in device memory owned by the handle and runs the device path.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -151,36 +152,126 @@ extern "C" gs_status gs_host_gemm_ex(gs_handle h, const gs_ex_desc *d) {
     uint8_t *dA = static_cast<uint8_t *>(ctx.stage);
     uint8_t *dB = dA + off_b;
     uint8_t *dC = dA + off_c;
-    cudaStream_t s = ctx.stream;
     // C is uploaded whenever it is read (beta != 0) or has bytes between its
     // elements that the download must leave untouched.
     const bool c_dense = (d->layout == GS_LAYOUT_COL_MAJOR ? d->ldc == d->m : d->ldc == d->n) &&
                          (d->batch_count == 1 || sc == c_ext);
     const bool upload_c = d->beta_re != 0.0 || !c_dense;
-    cudaError_t e = cudaMemcpyAsync(dA, d->a, a_bytes, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(dB, d->b, b_bytes, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess && upload_c) e = cudaMemcpyAsync(dC, d->c, c_bytes, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) {
-        ctx.last_error = std::string("host to device copy: ") + cudaGetErrorString(e);
-        return GS_STATUS_EXECUTION_FAILED;
-    }
-    // Row-major C = op(A) op(B) is column-major C^T = op(B)^T op(A)^T.
+
+    // Row-major C = op(A) op(B) is column-major C^T = op(B)^T op(A)^T: X, Y are
+    // the column-major operands of that problem, C' its column-major result.
     const bool rm = d->layout == GS_LAYOUT_ROW_MAJOR;
     const int m = static_cast<int>(rm ? d->n : d->m), n = static_cast<int>(rm ? d->m : d->n);
     const int opx = rm ? d->op_b : d->op_a, opy = rm ? d->op_a : d->op_b;
-    const void *X = rm ? static_cast<const void *>(dB) : dA;
-    const void *Y = rm ? static_cast<const void *>(dA) : dB;
+    uint8_t *dX = rm ? dB : dA, *dY = rm ? dA : dB;
+    const uint8_t *hX = static_cast<const uint8_t *>(rm ? d->b : d->a);
+    const uint8_t *hY = static_cast<const uint8_t *>(rm ? d->a : d->b);
+    const size_t esx = rm ? esb : esa, esy = rm ? esa : esb;
+    const size_t ext_x = rm ? b_ext : a_ext, ext_y = rm ? a_ext : b_ext;
     const int ldx = static_cast<int>(rm ? d->ldb : d->lda), ldy = static_cast<int>(rm ? d->lda : d->ldb);
-    const long long sx = static_cast<long long>(rm ? sb : sa), sy = static_cast<long long>(rm ? sa : sb);
+    const size_t sx = rm ? sb : sa, sy = rm ? sa : sb;
     const int tx = rm ? d->b_type : d->a_type, ty = rm ? d->a_type : d->b_type;
-    st = gs_gemm_strided_batched_ex(h, opx, opy, m, n, static_cast<int>(d->k), alpha, X, tx, ldx, sx, Y, ty, ldy, sy,
-                                    beta, dC, d->c_type, static_cast<int>(d->ldc), static_cast<long long>(sc),
-                                    static_cast<int>(d->batch_count), d->compute_type, d->algo);
-    if (st != GS_STATUS_SUCCESS) return st;
-    e = cudaMemcpyAsync(d->c, dC, c_bytes, cudaMemcpyDeviceToHost, s);
+    const size_t batch = d->batch_count;
+
+    // Pipeline: stream h2d uploads, the handle's stream computes, stream d2h
+    // downloads. C' is cut into chunks (column blocks of one GEMM, or ranges of
+    // batch entries); each chunk's kernel waits for its uploads and its
+    // download waits for its kernel, so copies in both directions overlap each
+    // other and the tensor cores.
+    cudaError_t e = cudaSuccess;
+    if (!ctx.h2d) {
+        e = cudaStreamCreateWithFlags(&ctx.h2d, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx.d2h, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx.ev_start, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx.ev_a, cudaEventDisableTiming);
+        for (int i = 0; e == cudaSuccess && i < gs::Context::kMaxChunks; ++i) {
+            e = cudaEventCreateWithFlags(&ctx.ev_in[i], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx.ev_out[i], cudaEventDisableTiming);
+        }
+        if (e != cudaSuccess) {
+            ctx.last_error = std::string("pipeline streams/events: ") + cudaGetErrorString(e);
+            return GS_STATUS_EXECUTION_FAILED;
+        }
+    }
+    const size_t units = batch > 1 ? batch : static_cast<size_t>(n);
+    const size_t align = batch > 1 ? 1 : 256;
+    const size_t total_bytes = a_bytes + b_bytes + c_bytes * (upload_c ? 2 : 1);
+    size_t chunks = total_bytes / (32u << 20);
+    chunks = std::max<size_t>(1, std::min<size_t>({chunks, static_cast<size_t>(gs::Context::kMaxChunks),
+                                                   (units + align - 1) / align}));
+    // Only a contiguous Y column block can be uploaded per chunk (op N); otherwise Y goes first, whole.
+    const bool y_chunked = batch == 1 && opy == GS_OP_N;
+    cudaStream_t s = ctx.stream;
+    auto h2d = [&](uint8_t *dst, const uint8_t *src, size_t bytes) {
+        if (e == cudaSuccess && bytes > 0) e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx.h2d);
+    };
+    if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_start, s);  // work already queued on the handle's stream
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx.h2d, ctx.ev_start, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx.d2h, ctx.ev_start, 0);
+    if (batch == 1) {
+        h2d(dX, hX, ext_x * esx);
+        if (!y_chunked) h2d(dY, hY, ext_y * esy);
+        if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_a, ctx.h2d);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ctx.ev_a, 0);
+    }
+    for (size_t j = 0; j < chunks && e == cudaSuccess; ++j) {
+        size_t u0 = units * j / chunks, u1 = units * (j + 1) / chunks;
+        if (j > 0) u0 = (u0 / align) * align;
+        if (j + 1 < chunks) u1 = (u1 / align) * align;
+        if (u1 <= u0) continue;
+        size_t c0, c1;  // byte range of C' this chunk covers
+        const uint8_t *X = dX, *Y = dY;
+        uint8_t *C = dC;
+        int nn = n, bb = static_cast<int>(batch);
+        if (batch == 1) {
+            c0 = u0 * d->ldc * esc;
+            c1 = ((u1 - 1) * d->ldc + static_cast<size_t>(m)) * esc;
+            if (y_chunked) {
+                const size_t y0 = u0 * ldy * esy, y1 = ext_y == 0 ? y0 : ((u1 - 1) * ldy + d->k) * esy;
+                h2d(dY + y0, hY + y0, y1 - y0);
+                Y = dY + y0;
+            } else {
+                Y = dY + u0 * esy;  // op T: column j of C' reads row j of the stored (n' x k) Y
+            }
+            C = dC + c0;
+            nn = static_cast<int>(u1 - u0);
+        } else {
+            const size_t x0 = u0 * sx * esx, x1 = ((u1 - 1) * sx + ext_x) * esx;
+            const size_t y0 = u0 * sy * esy, y1 = ((u1 - 1) * sy + ext_y) * esy;
+            if (ext_x) h2d(dX + x0, hX + x0, x1 - x0);
+            if (ext_y) h2d(dY + y0, hY + y0, y1 - y0);
+            c0 = u0 * sc * esc;
+            c1 = ((u1 - 1) * sc + c_ext) * esc;
+            X = dX + x0;
+            Y = dY + y0;
+            C = dC + c0;
+            bb = static_cast<int>(u1 - u0);
+        }
+        if (upload_c) h2d(dC + c0, static_cast<const uint8_t *>(d->c) + c0, c1 - c0);
+        if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_in[j], ctx.h2d);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ctx.ev_in[j], 0);
+        if (e != cudaSuccess) break;
+        st = gs_gemm_strided_batched_ex(h, opx, opy, m, nn, static_cast<int>(d->k), alpha, X, tx, ldx,
+                                        static_cast<long long>(sx), Y, ty, ldy, static_cast<long long>(sy), beta, C,
+                                        d->c_type, static_cast<int>(d->ldc), static_cast<long long>(sc), bb,
+                                        d->compute_type, d->algo);
+        if (st != GS_STATUS_SUCCESS) {
+            cudaStreamSynchronize(ctx.h2d);
+            return st;
+        }
+        e = cudaEventRecord(ctx.ev_out[j], s);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx.d2h, ctx.ev_out[j], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(static_cast<uint8_t *>(d->c) + c0, dC + c0, c1 - c0, cudaMemcpyDeviceToHost, ctx.d2h);
+    }
+    // Leave the handle's stream ordered after the downloads, then wait for all of it.
+    if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_start, ctx.d2h);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ctx.ev_start, 0);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
-        ctx.last_error = std::string("device to host copy: ") + cudaGetErrorString(e);
+        cudaStreamSynchronize(ctx.h2d);
+        cudaStreamSynchronize(ctx.d2h);
+        ctx.last_error = std::string("host-buffer pipeline: ") + cudaGetErrorString(e);
         return GS_STATUS_EXECUTION_FAILED;
     }
     return GS_STATUS_SUCCESS;
