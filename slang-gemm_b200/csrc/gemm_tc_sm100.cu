@@ -12,9 +12,11 @@
 //  - CG = 2 (default for M > 128): a cluster of two CTAs computes a 256 x 256
 //    tile with tcgen05.mma.cta_group::2. Each CTA loads 128 rows of A and 128
 //    of the 256 B columns, so per-SM operand traffic is 2/3 of the 1-SM tile;
+//    the wide variant (long K loops) computes 256 x 512 with two such MMAs per
+//    K step into all 512 TMEM columns, cutting operand traffic by another 1/4;
 //    CG = 1: one CTA computes a 128 x 256 tile;
 //  - 128 bytes of K per pipeline stage (64 f16/bf16 or 128 s8), 6 stages (CG 2)
-//    or 4 stages (CG 1);
+//    or 4 stages (CG 1 and the wide pair tile);
 //  - warp 0: TMA producer. Operand transposes live in the tensor maps: op(A)=N
 //    (M-contiguous) and op(B)=T (N-contiguous) are fetched as MN-major 128-byte
 //    swizzled panels, op(A)=T and op(B)=N as K-major panels, and the UMMA
@@ -24,7 +26,7 @@
 //    tcgen05.commit frees shared-memory stages and publishes accumulators
 //    (to both CTAs of the pair for CG 2);
 //  - warps 2..9: epilogue, two warps per TMEM lane quadrant, each draining
-//    half of the 256 accumulator columns. tcgen05.ld gives each thread one
+//    half of a 256-column accumulator (the wide tile's two halves in turn). tcgen05.ld gives each thread one
 //    accumulator row; with beta == 0 a warp stages 32 rows x 16 columns in
 //    shared memory (column-major, like C) and writes them with a TMA tensor
 //    store (L2 evict_first); otherwise the 32 lanes store 32 consecutive rows
@@ -43,7 +45,7 @@ namespace gs {
 namespace tc {
 
 constexpr int BM = 128;        // accumulator rows per CTA
-constexpr int BN = 256;        // accumulator columns per tile
+constexpr int BN = 256;        // accumulator columns per tcgen05.mma (and per tile unless wide)
 constexpr int BK_BYTES = 128;  // K bytes per stage
 constexpr int TMEM_COLS = 2 * BN;
 // Epilogue warps: two per TMEM lane quadrant, each draining half of the columns.
@@ -54,12 +56,23 @@ constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 // (evict_last: its A and B panels are re-read by many tiles), those of batched
 // calls use the normal policy (each batch entry's panels are short-lived).
 
-template <int CG>
+// WIDE (CG 2 only): the pair computes a 256 x 512 tile as two 256 x 256
+// tcgen05.mma per K step into one accumulator spanning all 512 TMEM columns.
+// A is then reused over twice the columns: 48 KiB of operands per 1024
+// tensor-core cycles instead of 32 KiB per 512, i.e. 3/4 of the L2 -> SM
+// traffic (and power) of the 256 x 256 tile. The price is the single
+// accumulator: the epilogue drains it in two 256-column halves, and the next
+// tile's MMAs into a half wait until that half is drained.
+template <int CG, bool WIDE>
 struct Cfg {
-    static constexpr int STAGES = CG == 2 ? 6 : 4;
-    static constexpr int B_ROWS = BN / CG;                 // B columns this CTA loads per tile
+    static constexpr int TILE_N = WIDE ? 2 * BN : BN;      // columns of one tile
+    static constexpr int NSUB = TILE_N / BN;               // tcgen05.mma per K step
+    static constexpr int STAGES = WIDE ? 4 : (CG == 2 ? 6 : 4);
+    static constexpr int B_BOX = BN / CG;                  // B columns per TMA box (one per sub-MMA)
+    static constexpr int B_ROWS = NSUB * B_BOX;            // B columns this CTA loads per tile
     static constexpr int A_STAGE = BM * BK_BYTES;          // 16 KiB
-    static constexpr int B_STAGE = B_ROWS * BK_BYTES;      // 16 KiB (CG 2) / 32 KiB (CG 1)
+    static constexpr int B_SUB = B_BOX * BK_BYTES;         // bytes of one B box
+    static constexpr int B_STAGE = B_ROWS * BK_BYTES;      // 16 KiB (CG 2) / 32 KiB (CG 1, CG 2 wide)
     static constexpr int STAGE = A_STAGE + B_STAGE;
     static constexpr int TILE_M = BM * CG;                 // rows of one (pair) tile
     // Epilogue staging for TMA stores: per epilogue warp two 32-row x 16-column x 4-byte blocks.
@@ -99,12 +112,14 @@ __device__ __forceinline__ void tile_coords(const TcArgs &a, long long t, int &b
     nb = within / gm;
 }
 
-template <int IN, int OUT, int CG>
+template <int IN, int OUT, int CG, bool WIDE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmC, const TcArgs args) {
-    using C_ = Cfg<CG>;
+    using C_ = Cfg<CG, WIDE>;
+    static_assert(!WIDE || CG == 2, "the wide tile is a CTA-pair tile");
     constexpr int STAGES = C_::STAGES;
+    constexpr int TILE_N = C_::TILE_N;
     constexpr int ES = (IN == IN_I8) ? 1 : 2;          // element bytes
     constexpr int BK = BK_BYTES / ES;                  // K elements per stage
     constexpr int UK = (IN == IN_I8) ? 32 : 16;        // K per tcgen05.mma
@@ -179,7 +194,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 int b, mb, nb;
                 tile_coords(args, t, b, mb, nb);
                 const int m0 = mb * C_::TILE_M + static_cast<int>(rank) * BM;
-                const int n0 = nb * BN + static_cast<int>(rank) * C_::B_ROWS;
+                // B box s feeds sub-MMA s (tile columns s*256 .. s*256+255); of those,
+                // this CTA of the pair holds columns rank*B_BOX .. rank*B_BOX+B_BOX-1.
+                const int n0 = nb * TILE_N + static_cast<int>(rank) * C_::B_BOX;
                 const CUtensorMap *ma = &tmA, *mbp = &tmB;
                 int ab = args.a_bcast ? 0 : b, bb = args.b_bcast ? 0 : b;
                 if (args.a_maps != nullptr) {
@@ -206,12 +223,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         } else {
                             tma_load_3d_2sm(dA, ma, fbar, k0, m0, ab, pol_ab);
                         }
-                        if (args.b_mn) {
 #pragma unroll
-                            for (int c = 0; c < C_::B_ROWS / CH; ++c)
-                                tma_load_3d_2sm(dB + c * CH_BYTES, mbp, fbar, n0 + c * CH, k0, bb, pol_ab);
-                        } else {
-                            tma_load_3d_2sm(dB, mbp, fbar, k0, n0, bb, pol_ab);
+                        for (int s = 0; s < C_::NSUB; ++s) {
+                            uint8_t *dBs = dB + s * C_::B_SUB;
+                            const int ns = n0 + s * BN;
+                            if (args.b_mn) {
+#pragma unroll
+                                for (int c = 0; c < C_::B_BOX / CH; ++c)
+                                    tma_load_3d_2sm(dBs + c * CH_BYTES, mbp, fbar, ns + c * CH, k0, bb, pol_ab);
+                            } else {
+                                tma_load_3d_2sm(dBs, mbp, fbar, k0, ns, bb, pol_ab);
+                            }
                         }
                     } else {
                         mbar_arrive_expect_tx(&full[stage], C_::STAGE);
@@ -242,9 +264,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t phase = 0;
             int it = 0;
             bool ok = true;
+            // Accumulator slots: two 256-column buffers used by alternate tiles, or
+            // (WIDE) the two halves of one 512-column accumulator used by every tile.
+            auto commit_to = [&](uint64_t *bar) {
+                if constexpr (CG == 2) umma_commit_2sm(bar, 0x3);
+                else umma_commit(bar);
+            };
             for (long long t = tile0; ok && t < args.total_tiles; t += tile_step, ++it) {
-                const int acc = it & 1;
-                const uint32_t acc_phase = (it >> 1) & 1;
+                const int acc = WIDE ? 0 : (it & 1);
+                const uint32_t acc_phase = WIDE ? (it & 1) : ((it >> 1) & 1);
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, 2)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
@@ -252,30 +280,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (!mbar_wait(&full[stage], phase, args.err, 3)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_base = smem_u32(smA + stage * C_::A_STAGE);
-                    const uint32_t b_base = smem_u32(smB + stage * C_::B_STAGE);
 #pragma unroll
-                    for (int kk = 0; kk < BK / UK; ++kk) {
-                        const uint64_t adesc = args.a_mn ? umma_smem_desc_sw128(a_base + kk * UK * 128, CH_BYTES, 1024)
-                                                         : umma_smem_desc_sw128(a_base + kk * UK * ES, 16, 1024);
-                        const uint64_t bdesc = args.b_mn ? umma_smem_desc_sw128(b_base + kk * UK * 128, CH_BYTES, 1024)
-                                                         : umma_smem_desc_sw128(b_base + kk * UK * ES, 16, 1024);
-                        const uint32_t accum = (kb | kk) != 0;
-                        if constexpr (CG == 2) {
-                            if constexpr (IN == IN_I8) umma_i8_2sm(d_tmem, adesc, bdesc, idesc, accum);
-                            else umma_f16_2sm(d_tmem, adesc, bdesc, idesc, accum);
-                        } else {
-                            if constexpr (IN == IN_I8) umma_i8(d_tmem, adesc, bdesc, idesc, accum);
-                            else umma_f16(d_tmem, adesc, bdesc, idesc, accum);
+                    for (int s = 0; s < C_::NSUB; ++s) {
+                        if (WIDE && s == 1 && kb == 0) {
+                            // The second half of the accumulator may still be draining.
+                            if (!mbar_wait(&tempty[1], acc_phase ^ 1u, args.err, 2)) { ok = false; break; }
+                            tc_fence_after();
                         }
+                        const uint32_t b_base = smem_u32(smB + stage * C_::B_STAGE + s * C_::B_SUB);
+#pragma unroll
+                        for (int kk = 0; kk < BK / UK; ++kk) {
+                            const uint64_t adesc = args.a_mn
+                                                       ? umma_smem_desc_sw128(a_base + kk * UK * 128, CH_BYTES, 1024)
+                                                       : umma_smem_desc_sw128(a_base + kk * UK * ES, 16, 1024);
+                            const uint64_t bdesc = args.b_mn
+                                                       ? umma_smem_desc_sw128(b_base + kk * UK * 128, CH_BYTES, 1024)
+                                                       : umma_smem_desc_sw128(b_base + kk * UK * ES, 16, 1024);
+                            const uint32_t accum = (kb | kk) != 0;
+                            const uint32_t d = d_tmem + s * BN;
+                            if constexpr (CG == 2) {
+                                if constexpr (IN == IN_I8) umma_i8_2sm(d, adesc, bdesc, idesc, accum);
+                                else umma_f16_2sm(d, adesc, bdesc, idesc, accum);
+                            } else {
+                                if constexpr (IN == IN_I8) umma_i8(d, adesc, bdesc, idesc, accum);
+                                else umma_f16(d, adesc, bdesc, idesc, accum);
+                            }
+                        }
+                        // Last K step: publish the first half as soon as its MMAs are issued,
+                        // so its drain overlaps the second half's last MMAs.
+                        if (WIDE && s == 0 && kb + 1 == args.k_blocks) commit_to(&tfull[0]);
                     }
-                    if constexpr (CG == 2) umma_commit_2sm(&empty[stage], 0x3);
-                    else umma_commit(&empty[stage]);
+                    if (!ok) break;
+                    commit_to(&empty[stage]);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
-                if (ok) {
-                    if constexpr (CG == 2) umma_commit_2sm(&tfull[acc], 0x3);
-                    else umma_commit(&tfull[acc]);
-                }
+                if (ok) commit_to(&tfull[WIDE ? 1 : acc]);
             }
         }
     } else {
@@ -288,19 +327,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint64_t pol_c = l2_policy_evict_first();
         int stg_flip = 0;
         int it = 0;
-        for (long long t = tile0; t < args.total_tiles; t += tile_step, ++it) {
+        bool ok = true;
+        for (long long t = tile0; ok && t < args.total_tiles; t += tile_step, ++it) {
             int b, mb, nb;
             tile_coords(args, t, b, mb, nb);
-            const int acc = it & 1;
-            const uint32_t acc_phase = (it >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], acc_phase, args.err, 4)) break;
-            tc_fence_after();
             const int m = mb * C_::TILE_M + static_cast<int>(rank) * BM + row;
-            const int n0 = nb * BN;
             void *Cb = args.C;
             if (args.c_arr != nullptr) Cb = args.c_arr[b];
             else Cb = static_cast<uint8_t *>(args.C) + static_cast<size_t>(b) * args.stride_c *
                                                         ((OUT == OUT_F16 || OUT == OUT_BF16) ? 2 : 4);
+            // One pass per accumulator slot this tile owns: the tile's 256-column
+            // buffer, or (WIDE) each half of the 512-column accumulator in turn.
+#pragma unroll 1
+            for (int half = 0; half < C_::NSUB; ++half) {
+            const int acc = WIDE ? half : (it & 1);
+            const uint32_t acc_phase = WIDE ? (it & 1) : ((it >> 1) & 1);
+            if (!mbar_wait(&tfull[acc], acc_phase, args.err, 4)) { ok = false; break; }
+            tc_fence_after();
+            const int n0 = nb * TILE_N + half * BN;  // tile column of this slot's first accumulator column
             const int ncols = min(BN, args.n - n0);
 #pragma unroll 1
             for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
@@ -365,6 +409,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if constexpr (CG == 2) mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
                 else mbar_arrive(&tempty[acc]);
             }
+            }  // accumulator slots of this tile
         }
         if (args.tma_store && lane == 0) bulk_wait_group_all();  // C is written before the kernel ends
     }
@@ -430,11 +475,11 @@ static int max_pairs(Context &ctx, K kern, int smem) {
     return n;
 }
 
-template <int IN, int OUT, int CG>
+template <int IN, int OUT, int CG, bool WIDE>
 static cudaError_t launch_kernel(Context &ctx, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tcm,
                                  const TcArgs &args) {
-    using C_ = Cfg<CG>;
-    auto kern = k_gemm_tc<IN, OUT, CG>;
+    using C_ = Cfg<CG, WIDE>;
+    auto kern = k_gemm_tc<IN, OUT, CG, WIDE>;
     static bool attr_set[64] = {};  // per instantiation and device
     cudaError_t e = cudaSuccess;
     if (ctx.device < 0 || ctx.device >= 64 || !attr_set[ctx.device]) {
@@ -469,24 +514,32 @@ static cudaError_t launch_kernel(Context &ctx, const CUtensorMap &ta, const CUte
     }
 }
 
-template <int CG>
+template <int CG, bool WIDE>
 static cudaError_t dispatch(Context &ctx, const GemmDesc &d, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tcm,
                             const TcArgs &args) {
     switch (d.in_kind) {
     case IN_F16:
-        if (d.out_kind == OUT_F32) return launch_kernel<IN_F16, OUT_F32, CG>(ctx, ta, tb, tcm, args);
-        if (d.out_kind == OUT_F16) return launch_kernel<IN_F16, OUT_F16, CG>(ctx, ta, tb, tcm, args);
+        if (d.out_kind == OUT_F32) return launch_kernel<IN_F16, OUT_F32, CG, WIDE>(ctx, ta, tb, tcm, args);
+        if (d.out_kind == OUT_F16) return launch_kernel<IN_F16, OUT_F16, CG, WIDE>(ctx, ta, tb, tcm, args);
         break;
     case IN_BF16:
-        if (d.out_kind == OUT_F32) return launch_kernel<IN_BF16, OUT_F32, CG>(ctx, ta, tb, tcm, args);
-        if (d.out_kind == OUT_BF16) return launch_kernel<IN_BF16, OUT_BF16, CG>(ctx, ta, tb, tcm, args);
+        if (d.out_kind == OUT_F32) return launch_kernel<IN_BF16, OUT_F32, CG, WIDE>(ctx, ta, tb, tcm, args);
+        if (d.out_kind == OUT_BF16) return launch_kernel<IN_BF16, OUT_BF16, CG, WIDE>(ctx, ta, tb, tcm, args);
         break;
     case IN_I8:
-        if (d.out_kind == OUT_I32) return launch_kernel<IN_I8, OUT_I32, CG>(ctx, ta, tb, tcm, args);
+        if (d.out_kind == OUT_I32) return launch_kernel<IN_I8, OUT_I32, CG, WIDE>(ctx, ta, tb, tcm, args);
         break;
     default: break;
     }
     return cudaErrorInvalidValue;
+}
+
+// Tile shape: 1 = 128 x 256 (one SM), 2 = 256 x 256 (CTA pair), 3 = 256 x 512 (CTA pair, wide).
+static cudaError_t dispatch_shape(int shape, Context &ctx, const GemmDesc &d, const CUtensorMap &ta,
+                                  const CUtensorMap &tb, const CUtensorMap &tcm, const TcArgs &args) {
+    if (shape == 3) return dispatch<2, true>(ctx, d, ta, tb, tcm, args);
+    if (shape == 2) return dispatch<2, false>(ctx, d, ta, tb, tcm, args);
+    return dispatch<1, false>(ctx, d, ta, tb, tcm, args);
 }
 
 static CUtensorMapDataType tmap_dtype(InKind k) {
@@ -538,17 +591,19 @@ static bool make_c_map(const GemmDesc &d, CUtensorMap *tcm) {
                           static_cast<uint64_t>(d.batch), s1, s2, 32, 16, nullptr, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-static TcArgs make_args(Context &ctx, const GemmDesc &d, int cg) {
+static TcArgs make_args(Context &ctx, const GemmDesc &d, int shape) {
+    const int cg = shape == 1 ? 1 : 2;
     const int es = static_cast<int>(in_elem_size(d.in_kind));
     const int bk = BK_BYTES / es;
     const int tile_m = BM * cg;
+    const int tile_n = shape == 3 ? 2 * BN : BN;
     TcArgs a{};
     a.m = d.m;
     a.n = d.n;
     a.k = d.k;
     a.batch = d.batch;
     a.m_blocks = (d.m + tile_m - 1) / tile_m;
-    a.n_blocks = (d.n + BN - 1) / BN;
+    a.n_blocks = (d.n + tile_n - 1) / tile_n;
     a.k_blocks = (d.k + bk - 1) / bk;
     a.tiles_per_batch = static_cast<long long>(a.m_blocks) * a.n_blocks;
     a.total_tiles = a.tiles_per_batch * d.batch;
@@ -571,21 +626,29 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int cg) {
     return a;
 }
 
-// CTA-group choice. The algo argument is honoured as a hint (CUBLAS_GEMM_ALGO0
-// = 1-SM 128 x 256 tile, CUBLAS_GEMM_ALGO1 = 2-SM 256 x 256 pair tile); any
-// other value picks the pair tile whenever M > 128 gives both CTAs rows.
-static int choose_cg(const Context &, const GemmDesc &d) {
+// Tile-shape choice. The algo argument is honoured as a hint
+// (CUBLAS_GEMM_ALGO0 = 1-SM 128 x 256 tile, ALGO1 = 2-SM 256 x 256 pair tile,
+// ALGO2 = 2-SM 256 x 512 wide pair tile); any other value picks the pair tile
+// whenever M > 128 gives both CTAs rows, and the wide pair tile when the
+// problem has more than one 256-column block and a K loop long enough
+// (>= 32 stages) to amortise the undoubled accumulator's drain.
+static int choose_shape(const Context &, const GemmDesc &d) {
     if (d.algo == 0) return 1;
     if (d.algo == 1) return 2;
-    return d.m > BM ? 2 : 1;
+    if (d.algo == 2) return 3;
+    if (d.m <= BM) return 1;
+    const int k_blocks = (d.k + BK_BYTES / static_cast<int>(in_elem_size(d.in_kind)) - 1) /
+                         (BK_BYTES / static_cast<int>(in_elem_size(d.in_kind)));
+    return (d.n > BN && k_blocks >= 32) ? 3 : 2;
 }
 
 }  // namespace tc
 
 cudaError_t launch_tc(Context &ctx, const GemmDesc &d) {
     using namespace tc;
-    const int cg = choose_cg(ctx, d);
-    TcArgs args = make_args(ctx, d, cg);
+    const int shape = choose_shape(ctx, d);
+    const int cg = shape == 1 ? 1 : 2;
+    TcArgs args = make_args(ctx, d, shape);
     CUtensorMap ta, tb;
     std::string why;
     if (!make_maps(d, d.A, d.B, args.a_bcast ? 1 : d.batch, args.b_bcast ? 1 : d.batch, BN / cg, &ta, &tb, &why)) {
@@ -594,14 +657,15 @@ cudaError_t launch_tc(Context &ctx, const GemmDesc &d) {
     }
     CUtensorMap tcm = ta;  // placeholder when the epilogue stores directly
     args.tma_store = make_c_map(d, &tcm) ? 1 : 0;
-    return cg == 2 ? dispatch<2>(ctx, d, ta, tb, tcm, args) : dispatch<1>(ctx, d, ta, tb, tcm, args);
+    return dispatch_shape(shape, ctx, d, ta, tb, tcm, args);
 }
 
 cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
                                 void *const *c_arr) {
     using namespace tc;
-    const int cg = choose_cg(ctx, d);
-    TcArgs args = make_args(ctx, d, cg);
+    const int shape = choose_shape(ctx, d);
+    const int cg = shape == 1 ? 1 : 2;
+    TcArgs args = make_args(ctx, d, shape);
     // Template maps over a placeholder (16-byte aligned, never dereferenced
     // through the template) with the per-batch geometry; the builder kernel
     // swaps in each batch entry's address.
@@ -641,7 +705,7 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     args.b_maps = maps_b;
     args.c_arr = c_arr;
     args.skip_flag = misaligned;
-    e = cg == 2 ? dispatch<2>(ctx, d, ta, tb, tcm, args) : dispatch<1>(ctx, d, ta, tb, tcm, args);
+    e = dispatch_shape(shape, ctx, d, ta, tb, tcm, args);
     if (e != cudaSuccess) return e;
     // Runs only when the builder raised the flag (it reads the same word).
     return launch_simt_if_flag(ctx, d, a_arr, b_arr, c_arr, misaligned);

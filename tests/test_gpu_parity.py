@@ -72,8 +72,9 @@ def run_case(handle, dt, op_a, op_b, m, n, k, alpha=1.0, beta=0.0, ct=None, pad=
 
 
 TC = {gs.R_16F: gs.KERNEL_TC_F16, gs.R_16BF: gs.KERNEL_TC_BF16, gs.R_8I: gs.KERNEL_TC_I8}
-# algo hint: 0 = 1-SM 128x256 tile, 1 = 2-SM 256x256 pair tile (results must not depend on it)
-TILES = [0, 1]
+# algo hint: 0 = 1-SM 128x256 tile, 1 = 2-SM 256x256 pair tile, 2 = 2-SM 256x512 wide pair tile
+# (results must not depend on it)
+TILES = [0, 1, 2]
 
 
 @pytest.mark.parametrize("algo", TILES)
