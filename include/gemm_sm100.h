@@ -232,6 +232,66 @@ gs_status gs_host_gemm_ex(gs_handle handle, const gs_ex_desc *desc);
  * calls and by the column split of one large GEMM. */
 gs_status gs_plan_shards(long long units, int parts, long long align, long long *offsets);
 
+/* ---------------------------------------------------------------------- */
+/* Single-process multi-GPU calls                                          */
+/* ---------------------------------------------------------------------- */
+/* No reference counterpart: slang-gemm drives one device
+ * (src/vulkan_runner.zig:1273-1299). These split the calls above over several
+ * GPUs of one box from ONE host thread, one stream per device, and return
+ * when every device is done. Neither split needs a reduction:
+ *  - batched calls: device devs[g] computes batch entries
+ *    [off[g], off[g+1]) with off = gs_plan_shards(batchCount, ngpu, 1);
+ *  - gs_gemm_ex_colsplit_multi: device devs[g] computes the column block
+ *    C[:, off[g]:off[g+1]] with off = gs_plan_shards(n, ngpu, GS_COLSPLIT_ALIGN),
+ *    reading all of A and the matching columns of op(B).
+ * Every pointer in A[], B[], C[] (and the device pointer arrays of the
+ * pointer-array call) is the base of the WHOLE problem's buffer on device
+ * devs[g] -- the same leading dimensions and strides as the single-GPU call --
+ * and that device reads and writes only its own shard, so a caller may fill
+ * just the shard region. No kernel reads another GPU's memory.
+ * gather_to: -1 leaves each block on its device; an index g into devs copies
+ * every other device's block of C into C[g] (NCCL point-to-point, loaded at
+ * run time); GS_GATHER_ALL does that for every device. Gathering needs a dense
+ * C (ldc == m and, when batched, strideC == m*n); otherwise it returns
+ * GS_STATUS_NOT_SUPPORTED before launching anything. alpha/beta are host
+ * pointers as in the single-GPU calls. The caller's current device is
+ * restored on return. */
+#define GS_MULTI_MAX_GPUS 64
+#define GS_GATHER_ALL (-2)
+#define GS_COLSPLIT_ALIGN 256
+
+typedef struct gs_multi *gs_multi_handle;
+
+/* Creates one gs_handle and one non-blocking stream per device in devs[0..ngpu). */
+gs_status gs_multi_create(gs_multi_handle *handle, int ngpu, const int *devs);
+gs_status gs_multi_destroy(gs_multi_handle handle);
+const char *gs_multi_last_error(gs_multi_handle handle);
+/* Per-device times (ms, CUDA events on each device's stream) of the last call:
+ * the GEMM alone and GEMM + gather. Either array may be NULL; each holds ngpu
+ * entries, 0 for a device that had no shard. */
+gs_status gs_multi_last_times(gs_multi_handle handle, float *gemm_ms, float *total_ms);
+
+gs_status gs_gemm_strided_batched_ex_multi(gs_multi_handle handle, int transa, int transb, int m, int n, int k,
+                                           const void *alpha, const void *const A[], int Atype, int lda,
+                                           long long strideA, const void *const B[], int Btype, int ldb,
+                                           long long strideB, const void *beta, void *const C[], int Ctype, int ldc,
+                                           long long strideC, int batchCount, int computeType, int algo,
+                                           int gather_to);
+
+/* Aarray[g] etc. are device-devs[g] arrays of batchCount device pointers
+ * (entries outside the device's shard are not read). No gather: the C
+ * matrices of a pointer-array call need not form one buffer. */
+gs_status gs_gemm_batched_ex_multi(gs_multi_handle handle, int transa, int transb, int m, int n, int k,
+                                   const void *alpha, const void *const *const Aarray[], int Atype, int lda,
+                                   const void *const *const Barray[], int Btype, int ldb, const void *beta,
+                                   void *const *const Carray[], int Ctype, int ldc, int batchCount, int computeType,
+                                   int algo);
+
+gs_status gs_gemm_ex_colsplit_multi(gs_multi_handle handle, int transa, int transb, int m, int n, int k,
+                                    const void *alpha, const void *const A[], int Atype, int lda,
+                                    const void *const B[], int Btype, int ldb, const void *beta, void *const C[],
+                                    int Ctype, int ldc, int computeType, int algo, int gather_to);
+
 #ifdef __cplusplus
 }
 #endif

@@ -110,6 +110,17 @@ def _load() -> ctypes.CDLL:
         "gs_host_gemm_ex": (st, [vp, ctypes.POINTER(ExDesc)]),
         "gs_plan_shards": (st, [ll, i, ll, ctypes.POINTER(ll)]),
         "gs_gemm_batched_ex_noalloc": (st, [vp, i, i, i, i, i, vp, vp, i, i, vp, i, i, vp, vp, i, i, i, i]),
+        "gs_multi_create": (st, [ctypes.POINTER(vp), i, ctypes.POINTER(i)]),
+        "gs_multi_destroy": (st, [vp]),
+        "gs_multi_last_error": (ctypes.c_char_p, [vp]),
+        "gs_multi_last_times": (st, [vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float)]),
+        "gs_gemm_strided_batched_ex_multi": (st, [vp, i, i, i, i, i, vp, ctypes.POINTER(vp), i, i, ll,
+                                                  ctypes.POINTER(vp), i, i, ll, vp, ctypes.POINTER(vp), i, i, ll,
+                                                  i, i, i, i]),
+        "gs_gemm_batched_ex_multi": (st, [vp, i, i, i, i, i, vp, ctypes.POINTER(vp), i, i, ctypes.POINTER(vp), i,
+                                          i, vp, ctypes.POINTER(vp), i, i, i, i, i]),
+        "gs_gemm_ex_colsplit_multi": (st, [vp, i, i, i, i, i, vp, ctypes.POINTER(vp), i, i, ctypes.POINTER(vp), i,
+                                           i, vp, ctypes.POINTER(vp), i, i, i, i, i]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -319,4 +330,86 @@ class Handle:
         s = _lib.gs_host_gemm_ex(self._h, ctypes.byref(d))
         if check:
             self._check(s, "gs_host_gemm_ex")
+        return s
+
+
+GATHER_NONE, GATHER_ALL = -1, -2  # gather_to values besides an index into devs
+COLSPLIT_ALIGN = 256              # GS_COLSPLIT_ALIGN
+
+
+class MultiHandle:
+    """gs_multi_create: one handle and stream per device of `devs`, driven from this thread.
+
+    Operand lists hold, per device, the base pointer of the whole problem's buffer on that device
+    (torch CUDA tensors or ints); each device reads and writes only its shard (batch range, or
+    column block for colsplit). Calls are synchronous."""
+
+    def __init__(self, devs):
+        self.devs = list(devs)
+        arr = (ctypes.c_int * len(self.devs))(*self.devs)
+        h = ctypes.c_void_p()
+        s = _lib.gs_multi_create(ctypes.byref(h), len(self.devs), arr)
+        if s != STATUS_SUCCESS:
+            raise GemmError(s, "gs_multi_create")
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.gs_multi_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def last_error(self) -> str:
+        return _lib.gs_multi_last_error(self._h).decode()
+
+    def last_times(self) -> tuple[list[float], list[float]]:
+        """Per-device (GEMM ms, GEMM + gather ms) of the last call."""
+        n = len(self.devs)
+        g, t = (ctypes.c_float * n)(), (ctypes.c_float * n)()
+        _lib.gs_multi_last_times(self._h, g, t)
+        return list(g), list(t)
+
+    def _check(self, s, what):
+        if s != STATUS_SUCCESS:
+            raise GemmError(s, what, self.last_error())
+
+    def _arr(self, xs):
+        if len(xs) != len(self.devs):
+            raise ValueError("one operand per device expected")
+        return (ctypes.c_void_p * len(xs))(*[_ptr(x) for x in xs])
+
+    def gemm_strided_batched_ex(self, transa, transb, m, n, k, alpha, A, atype, lda, sa, B, btype, ldb, sb, beta,
+                                C, ctype, ldc, sc, batch, compute, algo=GEMM_DEFAULT, gather_to=GATHER_NONE,
+                                check=True) -> int:
+        a, b = _scalar(compute, alpha), _scalar(compute, beta)
+        s = _lib.gs_gemm_strided_batched_ex_multi(self._h, transa, transb, m, n, k, ctypes.byref(a), self._arr(A),
+                                                  atype, lda, sa, self._arr(B), btype, ldb, sb, ctypes.byref(b),
+                                                  self._arr(C), ctype, ldc, sc, batch, compute, algo, gather_to)
+        if check:
+            self._check(s, "gs_gemm_strided_batched_ex_multi")
+        return s
+
+    def gemm_batched_ex(self, transa, transb, m, n, k, alpha, Aarr, atype, lda, Barr, btype, ldb, beta, Carr, ctype,
+                        ldc, batch, compute, algo=GEMM_DEFAULT, check=True) -> int:
+        a, b = _scalar(compute, alpha), _scalar(compute, beta)
+        s = _lib.gs_gemm_batched_ex_multi(self._h, transa, transb, m, n, k, ctypes.byref(a), self._arr(Aarr), atype,
+                                          lda, self._arr(Barr), btype, ldb, ctypes.byref(b), self._arr(Carr), ctype,
+                                          ldc, batch, compute, algo)
+        if check:
+            self._check(s, "gs_gemm_batched_ex_multi")
+        return s
+
+    def gemm_ex_colsplit(self, transa, transb, m, n, k, alpha, A, atype, lda, B, btype, ldb, beta, C, ctype, ldc,
+                         compute, algo=GEMM_DEFAULT, gather_to=GATHER_NONE, check=True) -> int:
+        a, b = _scalar(compute, alpha), _scalar(compute, beta)
+        s = _lib.gs_gemm_ex_colsplit_multi(self._h, transa, transb, m, n, k, ctypes.byref(a), self._arr(A), atype,
+                                           lda, self._arr(B), btype, ldb, ctypes.byref(b), self._arr(C), ctype, ldc,
+                                           compute, algo, gather_to)
+        if check:
+            self._check(s, "gs_gemm_ex_colsplit_multi")
         return s

@@ -130,3 +130,38 @@ def test_plan_shards_rejects_bad_args():
         gs.plan_shards(-1, 2)
     with pytest.raises(gs.GemmError):
         gs.plan_shards(8, 0)
+
+
+def test_multi_handle_argument_checks():
+    """gs_multi_* reject bad arguments before touching any device."""
+    L = gs.lib()
+    h = ctypes.c_void_p()
+    two = (ctypes.c_int * 2)(0, 0)
+    assert L.gs_multi_create(None, 1, two) == gs.STATUS_INVALID_VALUE
+    assert L.gs_multi_create(ctypes.byref(h), 0, two) == gs.STATUS_INVALID_VALUE
+    assert L.gs_multi_create(ctypes.byref(h), 1, None) == gs.STATUS_INVALID_VALUE
+    assert L.gs_multi_create(ctypes.byref(h), 2, two) == gs.STATUS_INVALID_VALUE       # duplicate device
+    neg = (ctypes.c_int * 1)(-1)
+    assert L.gs_multi_create(ctypes.byref(h), 1, neg) == gs.STATUS_INVALID_VALUE
+    assert L.gs_multi_create(ctypes.byref(h), 65, (ctypes.c_int * 65)(*range(65))) == gs.STATUS_INVALID_VALUE
+    assert not h.value
+    assert L.gs_multi_destroy(None) == gs.STATUS_NOT_INITIALIZED
+    assert L.gs_multi_last_times(None, None, None) == gs.STATUS_NOT_INITIALIZED
+    one = ctypes.c_float(1.0)
+    ptrs = (ctypes.c_void_p * 1)(ALIGNED)
+    assert L.gs_gemm_strided_batched_ex_multi(None, 0, 0, 4, 4, 4, ctypes.byref(one), ptrs, gs.R_16F, 4, 16, ptrs,
+                                              gs.R_16F, 4, 16, ctypes.byref(one), ptrs, gs.R_32F, 4, 16, 2,
+                                              gs.COMPUTE_32F, -1, -1) == gs.STATUS_NOT_INITIALIZED
+    assert L.gs_gemm_ex_colsplit_multi(None, 0, 0, 4, 4, 4, ctypes.byref(one), ptrs, gs.R_16F, 4, ptrs, gs.R_16F, 4,
+                                       ctypes.byref(one), ptrs, gs.R_32F, 4, gs.COMPUTE_32F, -1, -1) \
+        == gs.STATUS_NOT_INITIALIZED
+    assert L.gs_gemm_batched_ex_multi(None, 0, 0, 4, 4, 4, ctypes.byref(one), ptrs, gs.R_16F, 4, ptrs, gs.R_16F, 4,
+                                      ctypes.byref(one), ptrs, gs.R_32F, 4, 2, gs.COMPUTE_32F, -1) \
+        == gs.STATUS_NOT_INITIALIZED
+
+
+@pytest.mark.skipif(gpu_available(), reason="checks behaviour without a GPU")
+def test_multi_create_without_gpu_fails_cleanly():
+    with pytest.raises(gs.GemmError) as ei:
+        gs.MultiHandle([0])
+    assert ei.value.status == gs.STATUS_NOT_INITIALIZED
