@@ -288,10 +288,10 @@ def call(h, cfg: dict, A, B, C):
         h.sgemm(ta, tb, m, n, k, cfg["alpha"], A, lda, B, ldb, cfg["beta"], C, m)
     elif cfg["api"] == "strided":
         h.gemm_strided_batched_ex(ta, tb, m, n, k, cfg["alpha"], A, cfg["dt"], lda, m * k, B, cfg["dt"], ldb, k * n,
-                                  cfg["beta"], C, cfg["ct"], m, m * n, b, cfg["comp"])
+                                  cfg["beta"], C, cfg["ct"], m, m * n, b, cfg["comp"], algo=cfg.get("algo", -1))
     else:
         h.gemm_ex(ta, tb, m, n, k, cfg["alpha"], A, cfg["dt"], lda, B, cfg["dt"], ldb, cfg["beta"], C, cfg["ct"], m,
-                  cfg["comp"])
+                  cfg["comp"], algo=cfg.get("algo", -1))
 
 
 def call_host(h, cfg: dict, Ah, Bh, Ch):
@@ -315,7 +315,7 @@ def run_ours(args, cfg_name: str) -> None:
 
     import gemm_sm100 as gs
 
-    cfg0 = CONFIGS[cfg_name]
+    cfg0 = dict(CONFIGS[cfg_name], algo=args.algo)
     rank, world, local, dist = dist_setup(args.gpus)
     cfg, shard = rank_share(cfg0, rank, world, args.scaling)
     peaks = load_peaks()
@@ -440,6 +440,9 @@ def run_ours(args, cfg_name: str) -> None:
         del full
     if args.cublas and rank == 0:
         line["cublas"] = cublas_compare(cfg, A, B, args.steps, args.warmup)
+        if "ms" in line["cublas"]:
+            # the reference's shader_cublas_ratio (bench/gemm_perf.zig:206): our ms / cuBLAS ms, same rank-0 shard
+            line["shader_cublas_ratio"] = round(max_kernel_ms / line["cublas"]["ms"], 4)
     h.close()
     if dist is not None:
         dist.destroy_process_group()
@@ -448,33 +451,119 @@ def run_ours(args, cfg_name: str) -> None:
 
 
 def cublas_compare(cfg: dict, A, B, steps: int, warmup: int) -> dict:
-    """cuBLAS (through torch) on the same operands, for the shader_cublas_ratio column."""
+    """cuBLAS on the same operands and arguments (cublasGemmEx / cublasGemmStridedBatchedEx, as
+    slang-gemm's src/cublas.zig calls them), timed like our kernel, for shader_cublas_ratio."""
     import torch
 
-    m, n, k = cfg["m"], cfg["n"], cfg["k"]
-    if cfg["api"] != "ex" or cfg["op"] != (0, 0) or cfg["dt"] == 3:
-        return {"note": "cuBLAS comparison implemented for f16/bf16 N/N gemmEx only"}
-    a = A.view(k, m)  # column-major m x k == row-major k x m
-    b = B.view(n, k)
-    out = torch.empty(n, m, device="cuda", dtype=torch.float32)
-    try:
-        fn = lambda: torch.mm(b, a, out_dtype=torch.float32, out=out)  # noqa: E731
-        fn()
-        kind = "torch.mm(out_dtype=float32)"
-    except Exception:
-        fn = lambda: torch.mm(b, a)  # noqa: E731
-        kind = "torch.mm (f16 output)"
+    import cublas_ref
+
+    m, n, k, b = cfg["m"], cfg["n"], cfg["k"], cfg["batch"]
+    ta, tb = cfg["op"]
+    lda = m if ta == 0 else k
+    ldb = k if tb == 0 else n
+    C2 = torch.zeros(m * n * b, device="cuda", dtype=torch.int32 if cfg["ct"] == 10 else torch.float32)
+    stream = torch.cuda.current_stream()
+    cb = cublas_ref.Cublas(stream=stream)
+    fn = lambda: cb.gemm_strided_batched_ex(ta, tb, m, n, k, cfg["alpha"], A, cfg["dt"], lda, m * k, B, cfg["dt"],  # noqa
+                                            ldb, k * n, cfg["beta"], C2, cfg["ct"], m, m * n, b, cfg["comp"])
+    status = fn()
+    if status != 0:
+        return {"note": f"cublasGemmEx returned {status}", "version": cublas_ref.version_string()}
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(stream)
     for _ in range(steps):
         fn()
-    e1.record()
+    e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    return {"ms": round(ms, 4), "tflops": round(2.0 * m * n * k / ms / 1e9, 1), "call": kind}
+    cb.close()
+    unit = "TOP/s" if cfg["dt"] == 3 else "TFLOP/s"
+    return {"ms": round(ms, 4), "value": round(2.0 * m * n * k * b / ms / 1e9, 1), "unit": unit,
+            "call": "cublasGemmStridedBatchedEx" if b > 1 else "cublasGemmEx",
+            "version": cublas_ref.version_string()}
+
+
+def run_sustained(args, cfg_name: str) -> None:
+    """Power-capped steady state: libgemm_sm100 and cuBLAS each run back-to-back calls for `--sustained`
+    seconds (alternating, twice), with NVML clock / power / throttle-reason samples every 10 ms. Prints one
+    JSON line (mode "sustained"), not the contract line: it shows the clock each library settles at under the
+    1 kW cap, which a 50-step burst does not reach."""
+    import torch
+
+    import cublas_ref
+    import gemm_sm100 as gs
+
+    cfg = dict(CONFIGS[cfg_name], algo=args.algo)
+    torch.cuda.set_device(0)
+    A, B, C = make_inputs(cfg, seed=1)
+    stream = torch.cuda.current_stream()
+    h = gs.Handle(stream)
+    cb = cublas_ref.Cublas(stream=stream)
+    m, n, k, b = cfg["m"], cfg["n"], cfg["k"], cfg["batch"]
+    ta, tb = cfg["op"]
+    lda, ldb = (m if ta == 0 else k), (k if tb == 0 else n)
+    C2 = torch.zeros_like(C)
+    theirs = lambda: cb.gemm_strided_batched_ex(ta, tb, m, n, k, cfg["alpha"], A, cfg["dt"], lda, m * k, B,  # noqa
+                                                cfg["dt"], ldb, k * n, cfg["beta"], C2, cfg["ct"], m, m * n, b,
+                                                cfg["comp"])
+    ours = lambda: call(h, cfg, A, B, C)  # noqa: E731
+    flops = 2.0 * m * n * k * b
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        nvh = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+    except Exception:
+        pynvml = None
+    rows = []
+    for rep in range(2):
+        for name, fn in (("libgemm_sm100", ours), ("cuBLAS", theirs)):
+            fn()
+            torch.cuda.synchronize()
+            t0 = time.time()
+            fn()
+            torch.cuda.synchronize()
+            iters = max(5, int(args.sustained / max(time.time() - t0, 1e-4)))
+            samples, stop = [], threading.Event()
+
+            def sample():
+                while pynvml is not None and not stop.is_set():
+                    try:
+                        samples.append((pynvml.nvmlDeviceGetClockInfo(nvh, pynvml.NVML_CLOCK_SM),
+                                        pynvml.nvmlDeviceGetPowerUsage(nvh) / 1000.0,
+                                        pynvml.nvmlDeviceGetCurrentClocksEventReasons(nvh)))
+                    except Exception:
+                        pass
+                    stop.wait(0.01)
+
+            th = threading.Thread(target=sample, daemon=True)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            th.start()
+            e0.record(stream)
+            for _ in range(iters):
+                fn()
+            e1.record(stream)
+            e1.synchronize()
+            stop.set()
+            th.join()
+            ms = e0.elapsed_time(e1) / iters
+            mid = samples[len(samples) // 4: 3 * len(samples) // 4] or samples
+            reasons = 0
+            for s in mid:
+                reasons |= s[2]
+            med = lambda xs: sorted(xs)[len(xs) // 2] if xs else None  # noqa: E731
+            rows.append({"impl": name, "rep": rep, "calls": iters, "ms": round(ms, 4),
+                         "value": round(flops / ms / 1e9, 1), "sm_mhz_median": med([s[0] for s in mid]),
+                         "power_w_median": None if not mid else round(med([s[1] for s in mid]), 1),
+                         "reasons": [v for bit, v in ClockSampler.REASONS.items() if reasons & bit]})
+            time.sleep(1.0)
+    cb.close()
+    emit({"mode": "sustained", "config": {"name": cfg_name, "workload": cfg["label"]}, "seconds": args.sustained,
+          "unit": "TOP/s" if cfg["dt"] == 3 else "TFLOP/s", "cublas_version": cublas_ref.version_string(),
+          "rows": rows})
 
 
 # ---- CPU legs: the reference's scalar algorithm (oracle port) ----------------------
@@ -595,6 +684,99 @@ def emit(line: dict) -> None:
         os.write(_RESULT_FD, data)
 
 
+# ---- manifest rows (the reference's JSONL harness, bench/gemm_perf.zig) ----------------
+
+def _manifest_scalar_fn(case):
+    """CPU scalar column of a manifest row: the oracle (single thread) at the reference bench's capped sizes,
+    256 for classic sgemm and 128 for Ex rows, 2 batch entries for batched Ex rows
+    (bench/gemm_perf.zig:317-336, :618-637, :729-774)."""
+    import numpy as np
+
+    import manifest as mf
+    import perf_rows as pr
+
+    orc = _oracle()
+    s = case.shape
+    cap = 256 if case.api in mf.CLASSIC_APIS else 128
+    m, n, k = min(s.m, cap), min(s.n, cap), min(s.k, cap)
+    batch = 2 if case.api in ("gemm_batched_ex", "gemm_strided_batched_ex") else 1
+    ar, ac = pr.stored_dims(case.op_a, m, k)
+    br, bc = pr.stored_dims(case.op_b, k, n)
+    opa, opb = mf.OP_VALUE[case.op_a], mf.OP_VALUE[case.op_b]
+    at, bt, ct, comp = case.type_codes()
+    if case.api in mf.CLASSIC_APIS:
+        a, b, c = pr.fill_f32(ar * ac, 0.1), pr.fill_f32(br * bc, -0.2), pr.fill_f32(m * n, 0.3)
+        t0 = time.perf_counter()
+        rc = orc.sgemm(orc.COL_MAJOR, opa, opb, m, n, k, 1.0, a, ar, b, br, 0.0, c, m)
+        ms = (time.perf_counter() - t0) * 1e3
+    else:
+        sa, sb, sc = ar * ac, br * bc, m * n
+        if case.a_type == mf.R8I:
+            a, b = pr.fill_i8(sa * batch, 1), pr.fill_i8(sb * batch, -2)
+        elif case.a_type in (mf.R16F, mf.R16BF):
+            a, b = pr.fill_lowp16(sa * batch, case.a_type, 0.1), pr.fill_lowp16(sb * batch, case.a_type, -0.2)
+        else:
+            a, b = pr.fill_f32(sa * batch, 0.1), pr.fill_f32(sb * batch, -0.2)
+        c = {mf.R32I: np.zeros(sc * batch, np.int32), mf.R16F: np.zeros(sc * batch, np.uint16)}.get(
+            case.c_type, np.zeros(sc * batch, np.float32))
+        t0 = time.perf_counter()
+        rc = orc.gemm_ex(opa, opb, m, n, k, 1.0, a, at, ar, b, bt, br, 0.0, c, ct, m, compute_type=comp,
+                         layout=orc.COL_MAJOR, batch=batch, sa=sa, sb=sb, sc=sc)
+        ms = (time.perf_counter() - t0) * 1e3
+    if rc != 0:
+        return None
+    return ms, (m, n, k, batch)
+
+
+def run_manifest(args):
+    """JSONL rows + summary line of the reference's benchmark CLI (bench/gemm_perf.zig:50-89), for this backend:
+    shader_* columns are libgemm_sm100, cublas_* the vendor library on the same buffers, scalar_* the oracle."""
+    import torch
+
+    import manifest as mf
+    import perf_rows as pr
+
+    if not torch.cuda.is_available():
+        emit({"status": "invalid", "error": "no CUDA device available"})
+        return 0
+    if args.device_substr:
+        names = [torch.cuda.get_device_name(i) for i in range(torch.cuda.device_count())]
+        idx = next((i for i, nm in enumerate(names) if args.device_substr in nm), None)
+        if idx is None:
+            emit({"status": "invalid", "error": f"no CUDA device name contains {args.device_substr!r}"})
+            return 1
+        torch.cuda.set_device(idx)
+    sizes = [int(x) for x in args.sizes.split(",") if x.strip()] if args.sizes else [512, 1024, 2048]
+    rects = []
+    for item in (args.rect_sizes or "").split(","):
+        if item.strip():
+            m, n, k = (int(v) for v in item.lower().split("x"))
+            rects.append(mf.Shape(m, n, k))
+    out = open(args.output, "w") if args.output else None
+
+    def write(row):
+        line = json.dumps(row)
+        if out:
+            out.write(line + "\n")
+            out.flush()
+        else:
+            emit(row)
+
+    runner = pr.Runner(write, warmup=args.warmup, iters=args.iters, fail_every_row=args.fail_every_row,
+                       only_cublas_supported=args.only_cublas_supported,
+                       tile_compatible_only=args.tile_compatible_only,
+                       scalar_fn=None if args.no_cpu_baseline else _manifest_scalar_fn)
+    summary = runner.run(sizes, rects, args.manifest == "all")
+    if out:
+        out.close()
+    geo = summary.geomean()
+    if args.fail_on_regression and geo is not None and geo > 1.0:
+        return 1
+    if args.fail_every_row and summary.strict_failures:
+        return 1
+    return 0
+
+
 def main():
     global _RESULT_FD
     sys.stdout.flush()
@@ -608,14 +790,41 @@ def main():
     ap.add_argument("--config", default="c3-f16-nn", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
-    ap.add_argument("--cublas", action="store_true", help="also time cuBLAS (torch.mm) on the same operands")
+    ap.add_argument("--no-cublas", dest="cublas", action="store_false",
+                    help="skip timing cuBLAS on the same operands (shader_cublas_ratio)")
+    ap.add_argument("--cublas", dest="cublas", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--gather", action="store_true", help="N > 1: also time an NCCL all-gather of C (separately)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the cpu_baseline sample")
     ap.add_argument("--ref-seconds", type=float, default=90.0, help="target total length of --impl reference")
+    ap.add_argument("--algo", type=int, default=-1,
+                    help="cublasGemmAlgo_t passed to every call (a tile hint: 0 = 128x256, 1 = 256x256 pair, "
+                         "2 = 256x512 pair; -1 = automatic)")
+    ap.add_argument("--sustained", type=float, default=0.0, metavar="SECONDS",
+                    help="instead of the contract line: power-capped steady state of this library vs cuBLAS")
+    rows = ap.add_argument_group("manifest rows (the reference's JSONL benchmark CLI; any of these selects it)")
+    rows.add_argument("--manifest", default=None, help="'all': every API/op/type case (bench/gemm_perf.zig:91)")
+    rows.add_argument("--sizes", default=None, help="comma-separated square sizes (default 512,1024,2048)")
+    rows.add_argument("--rect-sizes", default=None, help="comma-separated MxNxK shapes")
+    rows.add_argument("--iters", type=int, default=20, help="timed calls per row")
+    rows.add_argument("--fail-on-regression", action="store_true")
+    rows.add_argument("--fail-every-row", action="store_true")
+    rows.add_argument("--only-cublas-supported", action="store_true")
+    rows.add_argument("--tile-compatible-only", action="store_true")
+    rows.add_argument("--output", default=None, help="write rows to this file instead of stdout")
+    rows.add_argument("--device-substr", default=None, help="first CUDA device whose name contains this")
+    for accepted in ("--suite", "--ops", "--types"):
+        rows.add_argument(accepted, default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    row_mode = any(v is not None for v in (args.manifest, args.sizes, args.rect_sizes)) or args.fail_every_row or \
+        args.fail_on_regression or args.only_cublas_supported or args.tile_compatible_only
+    if row_mode:
+        sys.exit(run_manifest(args))
+    if args.sustained:
+        run_sustained(args, args.config)
+        return
     if args.impl == "reference":
         run_reference(args, args.config)
     else:

@@ -37,6 +37,8 @@ def _load():
     lib.cublasGemmStridedBatchedEx.argtypes = [vp, i, i, i, i, i, vp, vp, i, i, ll, vp, i, i, ll, vp, vp, i, i, ll,
                                                i, i, i]
     lib.cublasSgemm_v2.argtypes = [vp, i, i, i, i, i, vp, vp, i, vp, i, vp, vp, i]
+    lib.cublasSgemmStridedBatched.argtypes = [vp, i, i, i, i, i, vp, vp, i, ll, vp, i, ll, vp, vp, i, ll, i]
+    lib.cublasGemmBatchedEx.argtypes = [vp, i, i, i, i, i, vp, vp, i, i, vp, i, i, vp, vp, i, i, i, i, i]
     _lib = lib
     return lib
 
@@ -89,6 +91,25 @@ class Cublas:
         return _load().cublasGemmStridedBatchedEx(self._h, ta, tb, m, n, k, ctypes.byref(a), p(A), at, lda, sa, p(B),
                                                   bt, ldb, sb, ctypes.byref(b), p(C), ct, ldc, sc, batch, compute,
                                                   algo)
+
+
+    def sgemm(self, ta, tb, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, sa=0, sb=0, sc=0, batch=1) -> int:
+        """cublas.sgemm / sgemmStridedBatched (src/cublas.zig:171-226)."""
+        a, b = ctypes.c_float(alpha), ctypes.c_float(beta)
+        p = lambda x: x if isinstance(x, int) else x.data_ptr()  # noqa: E731
+        if batch == 1:
+            return _load().cublasSgemm_v2(self._h, ta, tb, m, n, k, ctypes.byref(a), p(A), lda, p(B), ldb,
+                                          ctypes.byref(b), p(C), ldc)
+        return _load().cublasSgemmStridedBatched(self._h, ta, tb, m, n, k, ctypes.byref(a), p(A), lda, sa, p(B), ldb,
+                                                 sb, ctypes.byref(b), p(C), ldc, sc, batch)
+
+    def gemm_batched_ex(self, ta, tb, m, n, k, alpha, Aarr, at, lda, Barr, bt, ldb, beta, Carr, ct, ldc, batch,
+                        compute, algo=-1) -> int:
+        """cublas.gemmBatchedEx (src/cublas.zig:239-241): device arrays of device pointers."""
+        a, b = self._scalar(compute, alpha), self._scalar(compute, beta)
+        p = lambda x: x if isinstance(x, int) else x.data_ptr()  # noqa: E731
+        return _load().cublasGemmBatchedEx(self._h, ta, tb, m, n, k, ctypes.byref(a), p(Aarr), at, lda, p(Barr), bt,
+                                           ldb, ctypes.byref(b), p(Carr), ct, ldc, batch, compute, algo)
 
 
 def version_string() -> str:
