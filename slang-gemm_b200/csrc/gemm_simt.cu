@@ -24,7 +24,8 @@ struct SimtArgs {
     const void *const *a_arr;
     const void *const *b_arr;
     void *const *c_arr;
-    const uint32_t *run_flag;  // when set: do the work only if *run_flag != 0
+    const uint32_t *run_flag;  // when set: do the work only if *run_flag == run_gen
+    uint32_t run_gen;
     Epilogue ep;
 };
 
@@ -41,7 +42,9 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const SimtArgs a) {
     using Acc = typename std::conditional<IN == IN_I8, int32_t, float>::type;
     __shared__ Acc As[TK][TM];
     __shared__ Acc Bs[TK][TN + 1];
-    if (a.run_flag != nullptr && *a.run_flag == 0u) return;
+    grid_dep_wait();
+    grid_dep_launch();
+    if (a.run_flag != nullptr && *a.run_flag != a.run_gen) return;
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
     const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN;
@@ -115,6 +118,8 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const SimtArgs a) {
 // k == 0: every output is alpha*0 + beta*old.
 template <int OUT>
 __global__ void k_scale(const SimtArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
     const long long per = static_cast<long long>(a.m) * a.n;
     const long long total = per * a.batch;
     for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < total;
@@ -131,7 +136,7 @@ __global__ void k_scale(const SimtArgs a) {
 }
 
 static SimtArgs make_args(const GemmDesc &d, const void *const *a_arr, const void *const *b_arr, void *const *c_arr,
-                          const uint32_t *flag) {
+                          const uint32_t *flag, uint32_t gen) {
     SimtArgs s{};
     s.trans_a = d.trans_a;
     s.trans_b = d.trans_b;
@@ -146,6 +151,7 @@ static SimtArgs make_args(const GemmDesc &d, const void *const *a_arr, const voi
     s.b_arr = b_arr;
     s.c_arr = c_arr;
     s.run_flag = flag;
+    s.run_gen = gen;
     s.ep = d.ep;
     return s;
 }
@@ -153,9 +159,9 @@ static SimtArgs make_args(const GemmDesc &d, const void *const *a_arr, const voi
 template <int IN, int OUT>
 static cudaError_t go(Context &ctx, const SimtArgs &s) {
     dim3 grid((s.m + TM - 1) / TM, (s.n + TN - 1) / TN, s.batch < 65535 ? s.batch : 65535);
-    k_gemm_simt<IN, OUT><<<grid, 256, 0, ctx.stream>>>(s);
+    const cudaError_t e = launch_pdl(k_gemm_simt<IN, OUT>, grid, dim3(256), 0, ctx.stream, 1, s);
     ctx.launches++;
-    return cudaGetLastError();
+    return e;
 }
 
 static cudaError_t dispatch(Context &ctx, const GemmDesc &d, const SimtArgs &s) {
@@ -172,29 +178,31 @@ static cudaError_t dispatch(Context &ctx, const GemmDesc &d, const SimtArgs &s) 
 
 cudaError_t launch_simt(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
                         void *const *c_arr) {
-    return simt::dispatch(ctx, d, simt::make_args(d, a_arr, b_arr, c_arr, nullptr));
+    return simt::dispatch(ctx, d, simt::make_args(d, a_arr, b_arr, c_arr, nullptr, 0u));
 }
 
 cudaError_t launch_simt_if_flag(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
-                                void *const *c_arr, const uint32_t *flag) {
-    return simt::dispatch(ctx, d, simt::make_args(d, a_arr, b_arr, c_arr, flag));
+                                void *const *c_arr, const uint32_t *flag, uint32_t gen) {
+    return simt::dispatch(ctx, d, simt::make_args(d, a_arr, b_arr, c_arr, flag, gen));
 }
 
 cudaError_t launch_scale(Context &ctx, const GemmDesc &d, void *const *c_arr) {
     using namespace simt;
-    const SimtArgs s = make_args(d, nullptr, nullptr, c_arr, nullptr);
+    const SimtArgs s = make_args(d, nullptr, nullptr, c_arr, nullptr, 0u);
     const long long total = static_cast<long long>(d.m) * d.n * d.batch;
     long long blocks = (total + 255) / 256;
     if (blocks > 4L * ctx.sm_count * 8) blocks = 4L * ctx.sm_count * 8;
     if (blocks < 1) blocks = 1;
+    const dim3 grid(static_cast<unsigned>(blocks));
+    cudaError_t e = cudaErrorInvalidValue;
     switch (d.out_kind) {
-    case OUT_F32: k_scale<OUT_F32><<<static_cast<unsigned>(blocks), 256, 0, ctx.stream>>>(s); break;
-    case OUT_F16: k_scale<OUT_F16><<<static_cast<unsigned>(blocks), 256, 0, ctx.stream>>>(s); break;
-    case OUT_BF16: k_scale<OUT_BF16><<<static_cast<unsigned>(blocks), 256, 0, ctx.stream>>>(s); break;
-    case OUT_I32: k_scale<OUT_I32><<<static_cast<unsigned>(blocks), 256, 0, ctx.stream>>>(s); break;
+    case OUT_F32: e = launch_pdl(k_scale<OUT_F32>, grid, dim3(256), 0, ctx.stream, 1, s); break;
+    case OUT_F16: e = launch_pdl(k_scale<OUT_F16>, grid, dim3(256), 0, ctx.stream, 1, s); break;
+    case OUT_BF16: e = launch_pdl(k_scale<OUT_BF16>, grid, dim3(256), 0, ctx.stream, 1, s); break;
+    case OUT_I32: e = launch_pdl(k_scale<OUT_I32>, grid, dim3(256), 0, ctx.stream, 1, s); break;
     }
     ctx.launches++;
-    return cudaGetLastError();
+    return e;
 }
 
 }  // namespace gs

@@ -93,7 +93,8 @@ struct TcArgs {
     void *const *c_arr;          // pointer-array batches: per-batch C
     const CUtensorMap *a_maps;   // pointer-array batches: per-batch maps in global memory
     const CUtensorMap *b_maps;
-    const uint32_t *skip_flag;   // pointer-array batches: set when a pointer is not 16-byte aligned
+    const uint32_t *skip_flag;   // pointer-array batches: == skip_gen when a pointer is not 16-byte aligned
+    uint32_t skip_gen;
     int tma_store;               // epilogue writes C with TMA tensor stores (beta == 0, C TMA-addressable)
     int ab_evict_last;           // operand loads use the evict_last L2 policy
     Epilogue ep;
@@ -144,10 +145,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;  // position in the CTA pair
     const bool leader = rank == 0;
 
+    grid_dep_wait();
+    grid_dep_launch();
     // Pointer-array batches whose pointers TMA cannot address are computed by
     // the CUDA-core kernel launched after this one instead. Every CTA reads
     // the same word, so both CTAs of a pair leave together.
-    if (args.skip_flag != nullptr && *args.skip_flag != 0u) return;
+    if (args.skip_flag != nullptr && *args.skip_flag == args.skip_gen) return;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -429,16 +432,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // a host-encoded template and patches the global address with
 // tensormap.replace, then makes the write visible to the tensor-map proxy.
 // A pointer that is not 16-byte aligned cannot be a TMA base address: the
-// builder then raises *misaligned, the tensor-core kernel returns at once and
-// the CUDA-core kernel computes the whole batch instead.
+// builder then writes this call's tag `gen` into *misaligned, the tensor-core
+// kernel returns at once and the CUDA-core kernel computes the whole batch
+// instead (a word tagged by an earlier call never matches).
 __global__ void k_build_ptr_maps(const CUtensorMap tmpl_a, const CUtensorMap tmpl_b, const void *const *a_arr,
                                  const void *const *b_arr, CUtensorMap *maps_a, CUtensorMap *maps_b, int batch,
-                                 uint32_t *misaligned) {
+                                 uint32_t *misaligned, uint32_t gen) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= batch) return;
     const uint64_t pa = reinterpret_cast<uint64_t>(a_arr[i]), pb = reinterpret_cast<uint64_t>(b_arr[i]);
     if (((pa | pb) & 15u) != 0u) {
-        atomicOr(misaligned, 1u);
+        atomicExch(misaligned, gen);
         return;
     }
     maps_a[i] = tmpl_a;
@@ -490,27 +496,16 @@ static cudaError_t launch_kernel(Context &ctx, const CUtensorMap &ta, const CUte
     if constexpr (CG == 2) {
         const long long pairs = args.total_tiles < max_pairs(ctx, kern, C_::SMEM) ? args.total_tiles
                                                                                  : max_pairs(ctx, kern, C_::SMEM);
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-        cfg.dynamicSmemBytes = C_::SMEM;
-        cfg.stream = ctx.stream;
-        cudaLaunchAttribute attr;
-        attr.id = cudaLaunchAttributeClusterDimension;
-        attr.val.clusterDim.x = 2;
-        attr.val.clusterDim.y = 1;
-        attr.val.clusterDim.z = 1;
-        cfg.attrs = &attr;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, args);
+        e = launch_pdl(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(NUM_THREADS), C_::SMEM, ctx.stream, 2, ta,
+                       tb, tcm, args);
         ctx.launches++;
-        if (e != cudaSuccess) return e;
-        return cudaGetLastError();
+        return e;
     } else {
         const long long grid = args.total_tiles < ctx.sm_count ? args.total_tiles : ctx.sm_count;
-        kern<<<static_cast<unsigned>(grid), NUM_THREADS, C_::SMEM, ctx.stream>>>(ta, tb, tcm, args);
+        e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(NUM_THREADS), C_::SMEM, ctx.stream, 1, ta, tb,
+                       tcm, args);
         ctx.launches++;
-        return cudaGetLastError();
+        return e;
     }
 }
 
@@ -690,14 +685,12 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     CUtensorMap *maps_a = static_cast<CUtensorMap *>(ctx.tmap_buf);
     CUtensorMap *maps_b = maps_a + d.batch;
     uint32_t *misaligned = ctx.dev_err + 1;
-    cudaError_t e0 = cudaMemsetAsync(misaligned, 0, sizeof(uint32_t), ctx.stream);
-    if (e0 != cudaSuccess) return e0;
+    const uint32_t gen = ctx.next_ptr_gen();
     const int threads = 128;
-    k_build_ptr_maps<<<(d.batch + threads - 1) / threads, threads, 0, ctx.stream>>>(ta, tb, a_arr, b_arr, maps_a,
-                                                                                     maps_b, d.batch, misaligned);
+    cudaError_t e = launch_pdl(k_build_ptr_maps, dim3((d.batch + threads - 1) / threads), dim3(threads), 0, ctx.stream,
+                               1, ta, tb, a_arr, b_arr, maps_a, maps_b, d.batch, misaligned, gen);
     ctx.launches++;
     ctx.last_kernels |= GS_KERNEL_TMAP;
-    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     args.a_bcast = 1;
     args.b_bcast = 1;
@@ -705,10 +698,11 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     args.b_maps = maps_b;
     args.c_arr = c_arr;
     args.skip_flag = misaligned;
+    args.skip_gen = gen;
     e = dispatch_shape(shape, ctx, d, ta, tb, tcm, args);
     if (e != cudaSuccess) return e;
-    // Runs only when the builder raised the flag (it reads the same word).
-    return launch_simt_if_flag(ctx, d, a_arr, b_arr, c_arr, misaligned);
+    // Runs only when the builder tagged the word with this call's value.
+    return launch_simt_if_flag(ctx, d, a_arr, b_arr, c_arr, misaligned, gen);
 }
 
 }  // namespace gs

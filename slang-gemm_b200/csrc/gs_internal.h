@@ -62,7 +62,48 @@ struct Context {
     // device copy of tensor maps for pointer-array batches
     void *tmap_buf = nullptr;
     size_t tmap_bytes = 0;
+    // Pointer-array calls tag the misalignment word with a per-call value
+    // instead of clearing it first (one stream operation less per call).
+    uint32_t ptr_gen = 0;
+    uint32_t next_ptr_gen() {
+        if (++ptr_gen == 0) ++ptr_gen;
+        return ptr_gen;
+    }
 };
+
+// Programmatic dependent launch: every kernel of this library starts with
+// griddepcontrol.wait (before touching global memory) and then lets its own
+// dependents be scheduled, so each launch may be issued before the previous
+// kernel in the stream has finished; the GPU overlaps the launch latency.
+#ifdef __CUDACC__
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+#endif
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+    if (cluster > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = static_cast<unsigned>(cluster);
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = static_cast<unsigned>(n);
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Args &&>(args)...);
+}
 
 // Validation + kernel choice for a strided (or single) GEMM; no device calls.
 gs_status plan_gemm(const GemmDesc &d, Plan *plan, std::string *why);
@@ -75,9 +116,9 @@ cudaError_t launch_ffma(Context &ctx, const GemmDesc &d);
 cudaError_t launch_simt(Context &ctx, const GemmDesc &d, const void *const *a_arr,
                         const void *const *b_arr, void *const *c_arr);
 cudaError_t launch_scale(Context &ctx, const GemmDesc &d, void *const *c_arr);
-// CUDA-core pointer-array GEMM that does its work only when *flag != 0.
+// CUDA-core pointer-array GEMM that does its work only when *flag == gen.
 cudaError_t launch_simt_if_flag(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
-                                void *const *c_arr, const uint32_t *flag);
+                                void *const *c_arr, const uint32_t *flag, uint32_t gen);
 
 // Tensor-map encoder obtained from the driver at run time.
 bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t dim0,

@@ -4,19 +4,26 @@
 // sgemm / sgemmStridedBatched (src/gemm.zig:286-317, :479-481). FP32 is not a
 // reduced-precision contraction, so it stays on the FMA pipes.
 //
-// CTA tile 128 x 128, K step 8, 256 threads, 8 x 8 outputs per thread held in
-// two 4x4 quadrants 64 rows / 64 columns apart (conflict-free float4 reads of
-// the shared-memory panels). Shared memory is double buffered and the next
-// K step's global loads are issued before the current step's FMAs. Interior
-// tiles with 16-byte aligned operands use float4 global loads and stores;
-// edge tiles and unaligned operands use guarded scalar accesses.
+// One kernel template, three CTA tiles chosen by problem size so that the grid
+// fills the 148 SMs:
+//   128 x 128 (256 threads, 8 x 8 outputs per thread)  large problems
+//    64 x  64 (256 threads, 4 x 4)                      medium
+//    32 x  32 ( 64 threads, 4 x 4)                      small
+// K step 16. Each thread's outputs are 4 x 4 blocks spaced BM/2 (BN/2) apart
+// when it holds 8 rows (columns), so its shared-memory reads are conflict-free
+// float4 loads. Shared memory is double buffered; the next K step's global
+// loads are issued before the current step's FMAs and stored after them, and
+// the operand fragments of step kk+1 are read from shared memory while step
+// kk's FMAs run. Interior tiles of 16-byte aligned operands use float4 global
+// loads and stores; edge tiles and unaligned operands use guarded scalar
+// accesses. Operands stored K-contiguous (A op T, B op N) are transposed into
+// the [k][m] / [k][n] shared layout with scalar stores into rows padded by 4
+// floats (at most 2-way bank conflicts).
 #include "gs_epilogue.cuh"
 #include "gs_internal.h"
 
 namespace gs {
 namespace ffma {
-
-constexpr int BM = 128, BN = 128, BK = 8;
 
 struct FfmaArgs {
     int m, n, k, batch;
@@ -27,91 +34,123 @@ struct FfmaArgs {
     Epilogue ep;
 };
 
-// Loads this thread's 4 elements of the A panel (128 rows x 8 k) starting at k0.
-//  op N: A[m + k*lda]  -> thread covers k = tid/32, m = (tid%32)*4 .. +3
-//  op T: A[k + m*lda]  -> thread covers m = tid/2,  k = (tid%2)*4 .. +3
-template <int TA>
-__device__ __forceinline__ void load_a(const FfmaArgs &a, const float *A, int m0, int k0, int tid, bool fast, float (&r)[4]) {
+template <int BM_, int BN_, int TM_, int TN_, int MINB_, int BK_ = 16>
+struct Tile {
+    static constexpr int BM = BM_, BN = BN_, BK = BK_, TM = TM_, TN = TN_, MINB = MINB_;
+    static constexpr int TX = BM / TM, TY = BN / TN;        // threads along M and N
+    static constexpr int THREADS = TX * TY;
+    static constexpr int RM = TM / 4, RN = TN / 4;          // 4 x 4 blocks per thread along M and N
+    static constexpr int CH_A = BM * BK / 4 / THREADS;      // float4 chunks of A per thread per K step
+    static constexpr int CH_B = BN * BK / 4 / THREADS;
+    static_assert(CH_A * THREADS * 4 == BM * BK && CH_B * THREADS * 4 == BN * BK, "tile / thread mismatch");
+};
+using TileL = Tile<128, 128, 8, 8, 1>;
+using TileM = Tile<64, 64, 4, 4, 2>;
+using TileS = Tile<32, 32, 4, 4, 4>;
+
+// Chunk c of the A tile (BM rows x BK k) as (row or k, offset) for the stored layout.
+//  op N (M-contiguous): c -> k = c / (BM/4), m = (c % (BM/4)) * 4 .. +3
+//  op T (K-contiguous): c -> m = c / (BK/4), k = (c % (BK/4)) * 4 .. +3
+template <int TA, class T>
+__device__ __forceinline__ void load_a(const FfmaArgs &a, const float *A, int m0, int k0, int c, bool fast, float4 &r) {
     if constexpr (TA == 0) {
-        const int kr = tid >> 5, mc = (tid & 31) * 4;
+        const int kr = c / (T::BM / 4), mc = (c % (T::BM / 4)) * 4;
         const float *p = A + static_cast<size_t>(k0 + kr) * a.lda + m0 + mc;
         if (fast) {
-            const float4 v = *reinterpret_cast<const float4 *>(p);
-            r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+            r = __ldg(reinterpret_cast<const float4 *>(p));
         } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) r[i] = (m0 + mc + i < a.m && k0 + kr < a.k) ? p[i] : 0.0f;
+            const bool kin = k0 + kr < a.k;
+            r.x = (kin && m0 + mc + 0 < a.m) ? p[0] : 0.0f;
+            r.y = (kin && m0 + mc + 1 < a.m) ? p[1] : 0.0f;
+            r.z = (kin && m0 + mc + 2 < a.m) ? p[2] : 0.0f;
+            r.w = (kin && m0 + mc + 3 < a.m) ? p[3] : 0.0f;
         }
     } else {
-        const int mr = tid >> 1, kc = (tid & 1) * 4;
+        const int mr = c / (T::BK / 4), kc = (c % (T::BK / 4)) * 4;
         const float *p = A + static_cast<size_t>(m0 + mr) * a.lda + k0 + kc;
         if (fast) {
-            const float4 v = *reinterpret_cast<const float4 *>(p);
-            r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+            r = __ldg(reinterpret_cast<const float4 *>(p));
         } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) r[i] = (m0 + mr < a.m && k0 + kc + i < a.k) ? p[i] : 0.0f;
+            const bool min_ = m0 + mr < a.m;
+            r.x = (min_ && k0 + kc + 0 < a.k) ? p[0] : 0.0f;
+            r.y = (min_ && k0 + kc + 1 < a.k) ? p[1] : 0.0f;
+            r.z = (min_ && k0 + kc + 2 < a.k) ? p[2] : 0.0f;
+            r.w = (min_ && k0 + kc + 3 < a.k) ? p[3] : 0.0f;
         }
     }
 }
 
-//  op N: B[k + n*ldb]  -> thread covers n = tid/2,  k = (tid%2)*4 .. +3
-//  op T: B[n + k*ldb]  -> thread covers k = tid/32, n = (tid%32)*4 .. +3
-template <int TB>
-__device__ __forceinline__ void load_b(const FfmaArgs &a, const float *B, int n0, int k0, int tid, bool fast, float (&r)[4]) {
+//  op N (K-contiguous): c -> n = c / (BK/4), k = (c % (BK/4)) * 4 .. +3
+//  op T (N-contiguous): c -> k = c / (BN/4), n = (c % (BN/4)) * 4 .. +3
+template <int TB, class T>
+__device__ __forceinline__ void load_b(const FfmaArgs &a, const float *B, int n0, int k0, int c, bool fast, float4 &r) {
     if constexpr (TB == 0) {
-        const int nr = tid >> 1, kc = (tid & 1) * 4;
+        const int nr = c / (T::BK / 4), kc = (c % (T::BK / 4)) * 4;
         const float *p = B + static_cast<size_t>(n0 + nr) * a.ldb + k0 + kc;
         if (fast) {
-            const float4 v = *reinterpret_cast<const float4 *>(p);
-            r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+            r = __ldg(reinterpret_cast<const float4 *>(p));
         } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) r[i] = (n0 + nr < a.n && k0 + kc + i < a.k) ? p[i] : 0.0f;
+            const bool nin = n0 + nr < a.n;
+            r.x = (nin && k0 + kc + 0 < a.k) ? p[0] : 0.0f;
+            r.y = (nin && k0 + kc + 1 < a.k) ? p[1] : 0.0f;
+            r.z = (nin && k0 + kc + 2 < a.k) ? p[2] : 0.0f;
+            r.w = (nin && k0 + kc + 3 < a.k) ? p[3] : 0.0f;
         }
     } else {
-        const int kr = tid >> 5, nc = (tid & 31) * 4;
+        const int kr = c / (T::BN / 4), nc = (c % (T::BN / 4)) * 4;
         const float *p = B + static_cast<size_t>(k0 + kr) * a.ldb + n0 + nc;
         if (fast) {
-            const float4 v = *reinterpret_cast<const float4 *>(p);
-            r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+            r = __ldg(reinterpret_cast<const float4 *>(p));
         } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) r[i] = (n0 + nc + i < a.n && k0 + kr < a.k) ? p[i] : 0.0f;
+            const bool kin = k0 + kr < a.k;
+            r.x = (kin && n0 + nc + 0 < a.n) ? p[0] : 0.0f;
+            r.y = (kin && n0 + nc + 1 < a.n) ? p[1] : 0.0f;
+            r.z = (kin && n0 + nc + 2 < a.n) ? p[2] : 0.0f;
+            r.w = (kin && n0 + nc + 3 < a.n) ? p[3] : 0.0f;
         }
     }
 }
 
-template <int TA>
-__device__ __forceinline__ void store_a(float (*As)[BM], int tid, const float (&r)[4]) {
+// Shared layouts: As[k][m] with row length LDA_S, Bs[k][n] with row length LDB_S.
+template <int TA, class T>
+__device__ __forceinline__ void store_a(float *As, int lds, int c, const float4 &r) {
     if constexpr (TA == 0) {
-        const int kr = tid >> 5, mc = (tid & 31) * 4;
-        *reinterpret_cast<float4 *>(&As[kr][mc]) = make_float4(r[0], r[1], r[2], r[3]);
+        const int kr = c / (T::BM / 4), mc = (c % (T::BM / 4)) * 4;
+        *reinterpret_cast<float4 *>(&As[kr * lds + mc]) = r;
     } else {
-        const int mr = tid >> 1, kc = (tid & 1) * 4;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) As[kc + i][mr] = r[i];
+        const int mr = c / (T::BK / 4), kc = (c % (T::BK / 4)) * 4;
+        As[(kc + 0) * lds + mr] = r.x;
+        As[(kc + 1) * lds + mr] = r.y;
+        As[(kc + 2) * lds + mr] = r.z;
+        As[(kc + 3) * lds + mr] = r.w;
     }
 }
 
-template <int TB>
-__device__ __forceinline__ void store_b(float (*Bs)[BN], int tid, const float (&r)[4]) {
+template <int TB, class T>
+__device__ __forceinline__ void store_b(float *Bs, int lds, int c, const float4 &r) {
     if constexpr (TB == 0) {
-        const int nr = tid >> 1, kc = (tid & 1) * 4;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) Bs[kc + i][nr] = r[i];
+        const int nr = c / (T::BK / 4), kc = (c % (T::BK / 4)) * 4;
+        Bs[(kc + 0) * lds + nr] = r.x;
+        Bs[(kc + 1) * lds + nr] = r.y;
+        Bs[(kc + 2) * lds + nr] = r.z;
+        Bs[(kc + 3) * lds + nr] = r.w;
     } else {
-        const int kr = tid >> 5, nc = (tid & 31) * 4;
-        *reinterpret_cast<float4 *>(&Bs[kr][nc]) = make_float4(r[0], r[1], r[2], r[3]);
+        const int kr = c / (T::BN / 4), nc = (c % (T::BN / 4)) * 4;
+        *reinterpret_cast<float4 *>(&Bs[kr * lds + nc]) = r;
     }
 }
 
-template <int TA, int TB>
-__global__ void __launch_bounds__(256, 2) k_sgemm_ffma(const FfmaArgs a) {
-    __shared__ __align__(16) float As[2][BK][BM];
-    __shared__ __align__(16) float Bs[2][BK][BN];
+template <int TA, int TB, class T>
+__global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaArgs a) {
+    constexpr int BM = T::BM, BN = T::BN, BK = T::BK, RM = T::RM, RN = T::RN;
+    constexpr int LDA_S = BM + (TA == 1 ? 4 : 0);   // padded when filled by transposing stores
+    constexpr int LDB_S = BN + (TB == 0 ? 4 : 0);
+    __shared__ __align__(16) float As[2][BK * LDA_S];
+    __shared__ __align__(16) float Bs[2][BK * LDB_S];
+    grid_dep_wait();
+    grid_dep_launch();
     const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;
+    const int tx = tid % T::TX, ty = tid / T::TX;
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
     const bool full_m = m0 + BM <= a.m, full_n = n0 + BN <= a.n;
     const int ktiles = (a.k + BK - 1) / BK;
@@ -121,19 +160,23 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_ffma(const FfmaArgs a) {
         const float *B = a.B + static_cast<size_t>(b) * a.stride_b;
         float *C = a.C + static_cast<size_t>(b) * a.stride_c;
 
-        float acc[8][8];
+        float acc[4 * RM][4 * RN];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 4 * RM; ++i)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+            for (int j = 0; j < 4 * RN; ++j) acc[i][j] = 0.0f;
 
-        float ra[4], rb[4];
+        float4 ra[T::CH_A], rb[T::CH_B];
         {
             const bool fk = BK <= a.k;
-            load_a<TA>(a, A, m0, 0, tid, a.vec_a && full_m && fk, ra);
-            load_b<TB>(a, B, n0, 0, tid, a.vec_b && full_n && fk, rb);
-            store_a<TA>(As[0], tid, ra);
-            store_b<TB>(Bs[0], tid, rb);
+#pragma unroll
+            for (int i = 0; i < T::CH_A; ++i) load_a<TA, T>(a, A, m0, 0, tid + i * T::THREADS, a.vec_a && full_m && fk, ra[i]);
+#pragma unroll
+            for (int i = 0; i < T::CH_B; ++i) load_b<TB, T>(a, B, n0, 0, tid + i * T::THREADS, a.vec_b && full_n && fk, rb[i]);
+#pragma unroll
+            for (int i = 0; i < T::CH_A; ++i) store_a<TA, T>(As[0], LDA_S, tid + i * T::THREADS, ra[i]);
+#pragma unroll
+            for (int i = 0; i < T::CH_B; ++i) store_b<TB, T>(Bs[0], LDB_S, tid + i * T::THREADS, rb[i]);
         }
         __syncthreads();
 
@@ -143,42 +186,67 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_ffma(const FfmaArgs a) {
             if (more) {
                 const int k0 = (kt + 1) * BK;
                 const bool fk = k0 + BK <= a.k;
-                load_a<TA>(a, A, m0, k0, tid, a.vec_a && full_m && fk, ra);
-                load_b<TB>(a, B, n0, k0, tid, a.vec_b && full_n && fk, rb);
+#pragma unroll
+                for (int i = 0; i < T::CH_A; ++i)
+                    load_a<TA, T>(a, A, m0, k0, tid + i * T::THREADS, a.vec_a && full_m && fk, ra[i]);
+#pragma unroll
+                for (int i = 0; i < T::CH_B; ++i)
+                    load_b<TB, T>(a, B, n0, k0, tid + i * T::THREADS, a.vec_b && full_n && fk, rb[i]);
             }
+            const float *as = As[cur];
+            const float *bs = Bs[cur];
+            float4 fa[2][RM], fb[2][RN];
+#pragma unroll
+            for (int r = 0; r < RM; ++r) fa[0][r] = *reinterpret_cast<const float4 *>(&as[r * (BM / RM) + tx * 4]);
+#pragma unroll
+            for (int r = 0; r < RN; ++r) fb[0][r] = *reinterpret_cast<const float4 *>(&bs[r * (BN / RN) + ty * 4]);
 #pragma unroll
             for (int kk = 0; kk < BK; ++kk) {
-                const float4 a0 = *reinterpret_cast<const float4 *>(&As[cur][kk][tx * 4]);
-                const float4 a1 = *reinterpret_cast<const float4 *>(&As[cur][kk][64 + tx * 4]);
-                const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[cur][kk][ty * 4]);
-                const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[cur][kk][64 + ty * 4]);
-                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+                const int f = kk & 1;
+                if (kk + 1 < BK) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
+                    for (int r = 0; r < RM; ++r)
+                        fa[f ^ 1][r] = *reinterpret_cast<const float4 *>(&as[(kk + 1) * LDA_S + r * (BM / RM) + tx * 4]);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                    for (int r = 0; r < RN; ++r)
+                        fb[f ^ 1][r] = *reinterpret_cast<const float4 *>(&bs[(kk + 1) * LDB_S + r * (BN / RN) + ty * 4]);
+                }
+#pragma unroll
+                for (int i = 0; i < 4 * RM; ++i) {
+                    const float4 &va = fa[f][i / 4];
+                    const float av = (i & 3) == 0 ? va.x : (i & 3) == 1 ? va.y : (i & 3) == 2 ? va.z : va.w;
+#pragma unroll
+                    for (int j = 0; j < 4 * RN; ++j) {
+                        const float4 &vb = fb[f][j / 4];
+                        const float bv = (j & 3) == 0 ? vb.x : (j & 3) == 1 ? vb.y : (j & 3) == 2 ? vb.z : vb.w;
+                        acc[i][j] = fmaf(av, bv, acc[i][j]);
+                    }
+                }
             }
             if (more) {
-                store_a<TA>(As[cur ^ 1], tid, ra);
-                store_b<TB>(Bs[cur ^ 1], tid, rb);
+#pragma unroll
+                for (int i = 0; i < T::CH_A; ++i) store_a<TA, T>(As[cur ^ 1], LDA_S, tid + i * T::THREADS, ra[i]);
+#pragma unroll
+                for (int i = 0; i < T::CH_B; ++i) store_b<TB, T>(Bs[cur ^ 1], LDB_S, tid + i * T::THREADS, rb[i]);
             }
             __syncthreads();
         }
 
-        // Epilogue: rows m0 + {tx*4 .. +3, 64 + tx*4 .. +3}, columns n0 + {ty*4 .. +3, 64 + ty*4 .. +3}.
+        // Epilogue: rows m0 + r*(BM/RM) + tx*4 + {0..3}, columns n0 + s*(BN/RN) + ty*4 + {0..3}.
+        // alpha*acc then + beta*C with separate roundings, as gemm(f32) does (src/gemm.zig:523-544).
         const bool fast_c = a.vec_c && full_m && full_n;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int gn = n0 + (j < 4 ? ty * 4 + j : 64 + ty * 4 + (j - 4));
+        for (int j = 0; j < 4 * RN; ++j) {
+            const int gn = n0 + (j / 4) * (BN / RN) + ty * 4 + (j & 3);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int gm = m0 + h * 64 + tx * 4;
+            for (int r = 0; r < RM; ++r) {
+                const int gm = m0 + r * (BM / RM) + tx * 4;
                 float *p = C + static_cast<size_t>(gn) * a.ldc + gm;
                 if (fast_c) {
-                    float4 v = make_float4(acc[h * 4 + 0][j], acc[h * 4 + 1][j], acc[h * 4 + 2][j], acc[h * 4 + 3][j]);
+                    float4 v = make_float4(acc[r * 4 + 0][j], acc[r * 4 + 1][j], acc[r * 4 + 2][j], acc[r * 4 + 3][j]);
                     if (!a.ep.identity) {
-                        v.x *= a.ep.alpha_f; v.y *= a.ep.alpha_f; v.z *= a.ep.alpha_f; v.w *= a.ep.alpha_f;
+                        v.x = __fmul_rn(a.ep.alpha_f, v.x); v.y = __fmul_rn(a.ep.alpha_f, v.y);
+                        v.z = __fmul_rn(a.ep.alpha_f, v.z); v.w = __fmul_rn(a.ep.alpha_f, v.w);
                     }
                     if (!a.ep.beta_zero) {
                         const float4 o = *reinterpret_cast<const float4 *>(p);
@@ -191,23 +259,38 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_ffma(const FfmaArgs a) {
                 } else if (gn < a.n) {
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
-                        if (gm + i < a.m) store_facc<OUT_F32>(C, static_cast<size_t>(gn) * a.ldc + gm + i, acc[h * 4 + i][j], a.ep);
+                        if (gm + i < a.m) store_facc<OUT_F32>(C, static_cast<size_t>(gn) * a.ldc + gm + i, acc[r * 4 + i][j], a.ep);
                 }
             }
         }
     }
 }
 
-template <int TA, int TB>
+template <int TA, int TB, class T>
 static cudaError_t go(Context &ctx, const FfmaArgs &a) {
-    dim3 grid((a.m + BM - 1) / BM, (a.n + BN - 1) / BN, a.batch < 65535 ? a.batch : 65535);
-    k_sgemm_ffma<TA, TB><<<grid, 256, 0, ctx.stream>>>(a);
+    dim3 grid((a.m + T::BM - 1) / T::BM, (a.n + T::BN - 1) / T::BN, a.batch < 65535 ? a.batch : 65535);
+    const cudaError_t e = launch_pdl(k_sgemm_ffma<TA, TB, T>, grid, dim3(T::THREADS), 0, ctx.stream, 1, a);
     ctx.launches++;
-    return cudaGetLastError();
+    return e;
+}
+
+template <class T>
+static cudaError_t go_ops(Context &ctx, const GemmDesc &d, const FfmaArgs &a) {
+    if (!d.trans_a && !d.trans_b) return go<0, 0, T>(ctx, a);
+    if (!d.trans_a && d.trans_b) return go<0, 1, T>(ctx, a);
+    if (d.trans_a && !d.trans_b) return go<1, 0, T>(ctx, a);
+    return go<1, 1, T>(ctx, a);
+}
+
+template <class T>
+static long long ctas(const GemmDesc &d) {
+    return static_cast<long long>((d.m + T::BM - 1) / T::BM) * ((d.n + T::BN - 1) / T::BN) * d.batch;
 }
 
 }  // namespace ffma
 
+// Tile choice: the largest tile whose grid still gives every SM at least one
+// CTA; grids of the smallest tile for problems too small to fill the GPU.
 cudaError_t launch_ffma(Context &ctx, const GemmDesc &d) {
     using namespace ffma;
     FfmaArgs a{};
@@ -224,10 +307,10 @@ cudaError_t launch_ffma(Context &ctx, const GemmDesc &d) {
     a.vec_b = al16(d.B) && d.ldb % 4 == 0 && (!batched || d.stride_b % 4 == 0);
     a.vec_c = al16(d.C) && d.ldc % 4 == 0 && (!batched || d.stride_c % 4 == 0);
     a.ep = d.ep;
-    if (!d.trans_a && !d.trans_b) return go<0, 0>(ctx, a);
-    if (!d.trans_a && d.trans_b) return go<0, 1>(ctx, a);
-    if (d.trans_a && !d.trans_b) return go<1, 0>(ctx, a);
-    return go<1, 1>(ctx, a);
+    const long long sms = ctx.sm_count > 0 ? ctx.sm_count : 148;
+    if (ctas<TileL>(d) >= sms) return go_ops<TileL>(ctx, d, a);
+    if (ctas<TileM>(d) >= sms) return go_ops<TileM>(ctx, d, a);
+    return go_ops<TileS>(ctx, d, a);
 }
 
 }  // namespace gs

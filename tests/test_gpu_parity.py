@@ -25,11 +25,11 @@ def extent(rows, cols, ld):
 
 
 def run_case(handle, dt, op_a, op_b, m, n, k, alpha=1.0, beta=0.0, ct=None, pad=(0, 0, 0), batch=1,
-             stride_pad=(0, 0, 0), seed=0, expect_kernel=None, bcast_a=False, algo=gs.GEMM_DEFAULT):
+             stride_pad=(0, 0, 0), seed=0, expect_kernel=None, bcast_a=False, algo=gs.GEMM_DEFAULT, comp=None):
     """Runs one (strided-batched) gemmEx on the GPU and on the oracle; returns the kernel bits used."""
     rng = np.random.default_rng(seed)
     ct = OUT_OF[dt] if ct is None else ct
-    comp = COMPUTE[dt]
+    comp = COMPUTE[dt] if comp is None else comp
     ar, ac = (m, k) if op_a == 0 else (k, m)
     br, bc = (k, n) if op_b == 0 else (n, k)
     lda, ldb, ldc = max(1, ar) + pad[0], max(1, br) + pad[1], max(1, m) + pad[2]
@@ -356,3 +356,19 @@ def test_tma_store_epilogue_ragged(handle, dt, ct, algo):
     run_case(handle, dt, 0, 0, 37 * q, 45 * q, 9 * q, alpha=alpha, ct=ct, seed=60, expect_kernel=TC[dt], algo=algo)
     run_case(handle, dt, 1, 1, 19 * q, 13 * q, 5 * q, alpha=1.0, ct=ct, batch=3, stride_pad=(q, q, 8), seed=61,
              expect_kernel=TC[dt], algo=algo)
+
+
+@pytest.mark.parametrize("op_a,op_b", [(0, 0), (1, 1), (0, 1)])
+def test_fp32_fast_tf32_runs_exact_ffma(handle, op_a, op_b):
+    """COMPUTE_32F_FAST_TF32 permits (does not require) TF32 products: this backend computes it exactly on the
+    FFMA kernel, to the FP32 tolerance."""
+    run_case(handle, gs.R_32F, op_a, op_b, 192, 160, 96, alpha=1.5, beta=0.5, seed=70, expect_kernel=gs.KERNEL_FFMA,
+             comp=gs.COMPUTE_32F_FAST_TF32)
+
+
+@pytest.mark.parametrize("m,n,k", [(32, 32, 40), (96, 64, 33), (200, 136, 260), (1000, 1000, 64),
+                                   (2040, 1288, 72)])
+@pytest.mark.parametrize("op_a,op_b", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_sgemm_tile_sizes(handle, m, n, k, op_a, op_b):
+    """The FFMA kernel's three CTA tiles (32x32, 64x64, 128x128, chosen by grid size) on ragged shapes."""
+    run_case(handle, gs.R_32F, op_a, op_b, m, n, k, alpha=1.5, beta=0.5, seed=m + n + k, expect_kernel=gs.KERNEL_FFMA)
