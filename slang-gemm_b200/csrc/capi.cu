@@ -472,6 +472,9 @@ gs_status gs_gemm_batched_ex(gs_handle h, int transa, int transb, int m, int n, 
     if (tc_types && ld_ok) {
         e = launch_tc_ptr_array(ctx, d, Aarray, Barray, Carray);
         ctx.last_kernels |= (t.in == IN_F16 ? GS_KERNEL_TC_F16 : t.in == IN_BF16 ? GS_KERNEL_TC_BF16 : GS_KERNEL_TC_I8);
+    } else if (t.in == IN_F32) {
+        e = launch_ffma_ptr(ctx, d, Aarray, Barray, Carray);
+        ctx.last_kernels |= GS_KERNEL_FFMA;
     } else {
         e = launch_simt(ctx, d, Aarray, Barray, Carray);
         ctx.last_kernels |= GS_KERNEL_SIMT;

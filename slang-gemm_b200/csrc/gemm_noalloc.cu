@@ -119,6 +119,8 @@ extern "C" gs_status gs_gemm_batched_ex_noalloc(void *stream, int transa, int tr
             e = launch_scale(ctx, d, Carray);
         } else if (t.in != IN_F32 && (d.lda * es) % 16 == 0 && (d.ldb * es) % 16 == 0) {
             e = launch_tc_ptr_array(ctx, d, Aarray, Barray, Carray);
+        } else if (t.in == IN_F32) {
+            e = launch_ffma_ptr(ctx, d, Aarray, Barray, Carray);
         } else {
             e = launch_simt(ctx, d, Aarray, Barray, Carray);
         }

@@ -113,6 +113,8 @@ cudaError_t launch_tc(Context &ctx, const GemmDesc &d);
 cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *const *a_arr,
                                 const void *const *b_arr, void *const *c_arr);
 cudaError_t launch_ffma(Context &ctx, const GemmDesc &d);
+cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
+                            void *const *c_arr);
 cudaError_t launch_simt(Context &ctx, const GemmDesc &d, const void *const *a_arr,
                         const void *const *b_arr, void *const *c_arr);
 cudaError_t launch_scale(Context &ctx, const GemmDesc &d, void *const *c_arr);

@@ -6,10 +6,13 @@
 //
 // One kernel template, three CTA tiles chosen by problem size so that the grid
 // fills the 148 SMs:
-//   128 x 128 (256 threads, 8 x 8 outputs per thread)  large problems
-//    64 x  64 (256 threads, 4 x 4)                      medium
-//    32 x  32 ( 64 threads, 4 x 4)                      small
-// K step 16. Each thread's outputs are 4 x 4 blocks spaced BM/2 (BN/2) apart
+//   128 x 128 (256 threads, 8 x 8 outputs per thread, 2 CTAs per SM)  large
+//    64 x  64 (128 threads, 4 x 8, 4 CTAs per SM)                      medium
+//    32 x  32 ( 64 threads, 4 x 4)                                     small
+// K step 16. The FMAs are Blackwell's packed FP32 FMA (FFMA2, __ffma2_rn):
+// one instruction updates two rows of an output column, which halves the
+// FMA instruction count — a kernel issuing one FFMA per cycle per scheduler is
+// issue-bound below the FMA pipe's rate, the packed form is not. Each thread's outputs are 4 x 4 blocks spaced BM/2 (BN/2) apart
 // when it holds 8 rows (columns), so its shared-memory reads are conflict-free
 // float4 loads. Shared memory is double buffered; the next K step's global
 // loads are issued before the current step's FMAs and stored after them, and
@@ -30,7 +33,10 @@ struct FfmaArgs {
     const float *A; long long lda, stride_a;
     const float *B; long long ldb, stride_b;
     float *C; long long ldc, stride_c;
-    int vec_a, vec_b, vec_c;  // operand allows float4 access along its contiguous dimension
+    int vec_a, vec_b, vec_c;  // leading dimension / stride allow float4 access along the contiguous dimension
+    const float *const *a_arr;  // pointer-array batches (else nullptr): per-entry A, B, C
+    const float *const *b_arr;
+    float *const *c_arr;
     Epilogue ep;
 };
 
@@ -44,8 +50,8 @@ struct Tile {
     static constexpr int CH_B = BN * BK / 4 / THREADS;
     static_assert(CH_A * THREADS * 4 == BM * BK && CH_B * THREADS * 4 == BN * BK, "tile / thread mismatch");
 };
-using TileL = Tile<128, 128, 8, 8, 1>;
-using TileM = Tile<64, 64, 4, 4, 2>;
+using TileL = Tile<128, 128, 8, 8, 2>;
+using TileM = Tile<64, 64, 4, 8, 4>;
 using TileS = Tile<32, 32, 4, 4, 4>;
 
 // Chunk c of the A tile (BM rows x BK k) as (row or k, offset) for the stored layout.
@@ -156,23 +162,27 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
     const int ktiles = (a.k + BK - 1) / BK;
 
     for (int b = blockIdx.z; b < a.batch; b += gridDim.z) {
-        const float *A = a.A + static_cast<size_t>(b) * a.stride_a;
-        const float *B = a.B + static_cast<size_t>(b) * a.stride_b;
-        float *C = a.C + static_cast<size_t>(b) * a.stride_c;
+        const float *A = a.a_arr ? a.a_arr[b] : a.A + static_cast<size_t>(b) * a.stride_a;
+        const float *B = a.b_arr ? a.b_arr[b] : a.B + static_cast<size_t>(b) * a.stride_b;
+        float *C = a.c_arr ? a.c_arr[b] : a.C + static_cast<size_t>(b) * a.stride_c;
+        // float4 accesses need this entry's base 16-byte aligned as well
+        const bool va = a.vec_a && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
+        const bool vb = a.vec_b && (reinterpret_cast<uintptr_t>(B) & 15u) == 0;
+        const bool vc = a.vec_c && (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
 
-        float acc[4 * RM][4 * RN];
+        float2 acc2[2 * RM][4 * RN];  // acc2[ip][j] = outputs (rows 2ip, 2ip+1 of this thread, column j)
 #pragma unroll
-        for (int i = 0; i < 4 * RM; ++i)
+        for (int i = 0; i < 2 * RM; ++i)
 #pragma unroll
-            for (int j = 0; j < 4 * RN; ++j) acc[i][j] = 0.0f;
+            for (int j = 0; j < 4 * RN; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
 
         float4 ra[T::CH_A], rb[T::CH_B];
         {
             const bool fk = BK <= a.k;
 #pragma unroll
-            for (int i = 0; i < T::CH_A; ++i) load_a<TA, T>(a, A, m0, 0, tid + i * T::THREADS, a.vec_a && full_m && fk, ra[i]);
+            for (int i = 0; i < T::CH_A; ++i) load_a<TA, T>(a, A, m0, 0, tid + i * T::THREADS, va && full_m && fk, ra[i]);
 #pragma unroll
-            for (int i = 0; i < T::CH_B; ++i) load_b<TB, T>(a, B, n0, 0, tid + i * T::THREADS, a.vec_b && full_n && fk, rb[i]);
+            for (int i = 0; i < T::CH_B; ++i) load_b<TB, T>(a, B, n0, 0, tid + i * T::THREADS, vb && full_n && fk, rb[i]);
 #pragma unroll
             for (int i = 0; i < T::CH_A; ++i) store_a<TA, T>(As[0], LDA_S, tid + i * T::THREADS, ra[i]);
 #pragma unroll
@@ -188,10 +198,10 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
                 const bool fk = k0 + BK <= a.k;
 #pragma unroll
                 for (int i = 0; i < T::CH_A; ++i)
-                    load_a<TA, T>(a, A, m0, k0, tid + i * T::THREADS, a.vec_a && full_m && fk, ra[i]);
+                    load_a<TA, T>(a, A, m0, k0, tid + i * T::THREADS, va && full_m && fk, ra[i]);
 #pragma unroll
                 for (int i = 0; i < T::CH_B; ++i)
-                    load_b<TB, T>(a, B, n0, k0, tid + i * T::THREADS, a.vec_b && full_n && fk, rb[i]);
+                    load_b<TB, T>(a, B, n0, k0, tid + i * T::THREADS, vb && full_n && fk, rb[i]);
             }
             const float *as = As[cur];
             const float *bs = Bs[cur];
@@ -211,15 +221,18 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
                     for (int r = 0; r < RN; ++r)
                         fb[f ^ 1][r] = *reinterpret_cast<const float4 *>(&bs[(kk + 1) * LDB_S + r * (BN / RN) + ty * 4]);
                 }
+                // Packed FP32 FMA (FFMA2): two rows of one output column per instruction, each
+                // element rounded once exactly as fmaf rounds it.
 #pragma unroll
-                for (int i = 0; i < 4 * RM; ++i) {
-                    const float4 &va = fa[f][i / 4];
-                    const float av = (i & 3) == 0 ? va.x : (i & 3) == 1 ? va.y : (i & 3) == 2 ? va.z : va.w;
+                for (int j = 0; j < 4 * RN; ++j) {
+                    const float4 &vb = fb[f][j / 4];
+                    const float bv = (j & 3) == 0 ? vb.x : (j & 3) == 1 ? vb.y : (j & 3) == 2 ? vb.z : vb.w;
+                    const float2 b2 = make_float2(bv, bv);
 #pragma unroll
-                    for (int j = 0; j < 4 * RN; ++j) {
-                        const float4 &vb = fb[f][j / 4];
-                        const float bv = (j & 3) == 0 ? vb.x : (j & 3) == 1 ? vb.y : (j & 3) == 2 ? vb.z : vb.w;
-                        acc[i][j] = fmaf(av, bv, acc[i][j]);
+                    for (int ip = 0; ip < 2 * RM; ++ip) {
+                        const float4 &va = fa[f][ip / 2];
+                        const float2 a2 = (ip & 1) ? make_float2(va.z, va.w) : make_float2(va.x, va.y);
+                        acc2[ip][j] = __ffma2_rn(a2, b2, acc2[ip][j]);
                     }
                 }
             }
@@ -232,9 +245,17 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
             __syncthreads();
         }
 
+        float acc[4 * RM][4 * RN];
+#pragma unroll
+        for (int i = 0; i < 2 * RM; ++i)
+#pragma unroll
+            for (int j = 0; j < 4 * RN; ++j) {
+                acc[2 * i][j] = acc2[i][j].x;
+                acc[2 * i + 1][j] = acc2[i][j].y;
+            }
         // Epilogue: rows m0 + r*(BM/RM) + tx*4 + {0..3}, columns n0 + s*(BN/RN) + ty*4 + {0..3}.
         // alpha*acc then + beta*C with separate roundings, as gemm(f32) does (src/gemm.zig:523-544).
-        const bool fast_c = a.vec_c && full_m && full_n;
+        const bool fast_c = vc && full_m && full_n;
 #pragma unroll
         for (int j = 0; j < 4 * RN; ++j) {
             const int gn = n0 + (j / 4) * (BN / RN) + ty * 4 + (j & 3);
@@ -291,9 +312,15 @@ static long long ctas(const GemmDesc &d) {
 
 // Tile choice: the largest tile whose grid still gives every SM at least one
 // CTA; grids of the smallest tile for problems too small to fill the GPU.
-cudaError_t launch_ffma(Context &ctx, const GemmDesc &d) {
+// a_arr/b_arr/c_arr: device arrays of per-entry pointers (pointer-array
+// batches), or nullptr for the strided layout of `d`.
+cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
+                            void *const *c_arr) {
     using namespace ffma;
     FfmaArgs a{};
+    a.a_arr = reinterpret_cast<const float *const *>(a_arr);
+    a.b_arr = reinterpret_cast<const float *const *>(b_arr);
+    a.c_arr = reinterpret_cast<float *const *>(c_arr);
     a.m = d.m;
     a.n = d.n;
     a.k = d.k;
@@ -301,16 +328,17 @@ cudaError_t launch_ffma(Context &ctx, const GemmDesc &d) {
     a.A = static_cast<const float *>(d.A); a.lda = d.lda; a.stride_a = d.stride_a;
     a.B = static_cast<const float *>(d.B); a.ldb = d.ldb; a.stride_b = d.stride_b;
     a.C = static_cast<float *>(d.C); a.ldc = d.ldc; a.stride_c = d.stride_c;
-    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-    const bool batched = d.batch > 1;
-    a.vec_a = al16(d.A) && d.lda % 4 == 0 && (!batched || d.stride_a % 4 == 0);
-    a.vec_b = al16(d.B) && d.ldb % 4 == 0 && (!batched || d.stride_b % 4 == 0);
-    a.vec_c = al16(d.C) && d.ldc % 4 == 0 && (!batched || d.stride_c % 4 == 0);
+    const bool strided = d.batch > 1 && a_arr == nullptr;
+    a.vec_a = d.lda % 4 == 0 && (!strided || d.stride_a % 4 == 0);
+    a.vec_b = d.ldb % 4 == 0 && (!strided || d.stride_b % 4 == 0);
+    a.vec_c = d.ldc % 4 == 0 && (!strided || d.stride_c % 4 == 0);
     a.ep = d.ep;
     const long long sms = ctx.sm_count > 0 ? ctx.sm_count : 148;
     if (ctas<TileL>(d) >= sms) return go_ops<TileL>(ctx, d, a);
     if (ctas<TileM>(d) >= sms) return go_ops<TileM>(ctx, d, a);
     return go_ops<TileS>(ctx, d, a);
 }
+
+cudaError_t launch_ffma(Context &ctx, const GemmDesc &d) { return launch_ffma_ptr(ctx, d, nullptr, nullptr, nullptr); }
 
 }  // namespace gs

@@ -284,7 +284,7 @@ def test_pointer_array_batched(handle, dt, misalign, algo):
     for i in range(batch):
         assert_parity(to_host(dc[i]), refs[i], ct, dt if dt != gs.R_8I else gs.R_32F)
     if dt == gs.R_32F:
-        assert kern & gs.KERNEL_SIMT
+        assert kern & gs.KERNEL_FFMA
     else:
         assert kern & gs.KERNEL_TMAP and kern & TC[dt]
     assert handle.device_error() == 0
