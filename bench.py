@@ -130,6 +130,16 @@ def committed_traffic(name: str):
         return None
 
 
+def committed_pipe_utilization(name: str):
+    """Tensor-pipe (or FMA-pipe) utilisation of the dominant kernel for this configuration, from the committed
+    ncu summary (profiles/pipe_utilization.json), if any."""
+    p = os.path.join(ROOT, "profiles", "pipe_utilization.json")
+    try:
+        return json.load(open(p)).get(name)
+    except Exception:
+        return None
+
+
 # ---- clock sampling during the timed region --------------------------------
 
 class ClockSampler:
@@ -415,6 +425,7 @@ def run_ours(args, cfg_name: str) -> None:
                 "d2h_bytes_per_step": d2h * world, "ms_per_step": round(e2e_ms, 3),
                 "path": "gs_host_gemm_ex (pinned host buffers; H2D, kernel, D2H, stream sync per step)"},
         "roofline": roof,
+        "pipe_utilization": committed_pipe_utilization(cfg_name),
         "gpu_launches": int(launches),
         "clocks": clocks,
         "device_error_word": dev_err,

@@ -625,16 +625,29 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int shape) {
 // (CUBLAS_GEMM_ALGO0 = 1-SM 128 x 256 tile, ALGO1 = 2-SM 256 x 256 pair tile,
 // ALGO2 = 2-SM 256 x 512 wide pair tile); any other value picks the pair tile
 // whenever M > 128 gives both CTAs rows, and the wide pair tile when the
-// problem has more than one 256-column block and a K loop long enough
-// (>= 32 stages) to amortise the undoubled accumulator's drain.
+// problem has more than one 256-column block and either a K loop long enough
+// (>= 32 stages) to amortise the undoubled accumulator's drain, or an
+// arithmetic intensity below the B200's tensor / HBM ridge (~260 flop/byte
+// for 16-bit inputs, ~520 op/byte for INT8), where the wide tile's smaller
+// operand traffic is worth more than the drain it exposes. (Measured: the wide
+// tile wins at 8192^3 and 4096^3 and for batch-256 512x512x1024 FP16; the
+// 256 x 256 tile wins for batch-64 2048^3 INT8, whose epilogue is busy 2/3 of
+// the time.)
 static int choose_shape(const Context &, const GemmDesc &d) {
     if (d.algo == 0) return 1;
     if (d.algo == 1) return 2;
     if (d.algo == 2) return 3;
     if (d.m <= BM) return 1;
-    const int k_blocks = (d.k + BK_BYTES / static_cast<int>(in_elem_size(d.in_kind)) - 1) /
-                         (BK_BYTES / static_cast<int>(in_elem_size(d.in_kind)));
-    return (d.n > BN && k_blocks >= 32) ? 3 : 2;
+    if (d.n <= BN) return 2;
+    const double es = static_cast<double>(in_elem_size(d.in_kind));
+    const int k_blocks = (d.k + BK_BYTES / static_cast<int>(es) - 1) / (BK_BYTES / static_cast<int>(es));
+    if (k_blocks >= 32) return 3;
+    const double m = d.m, n = d.n, k = d.k;
+    const double flops = 2.0 * m * n * k;
+    const double bytes = m * k * es + k * n * es + m * n * static_cast<double>(out_elem_size(d.out_kind)) *
+                                                        (d.ep.beta_zero ? 1.0 : 2.0);
+    const double ridge = d.in_kind == IN_I8 ? 520.0 : 260.0;
+    return flops / bytes < ridge ? 3 : 2;
 }
 
 }  // namespace tc
