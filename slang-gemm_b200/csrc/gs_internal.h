@@ -56,7 +56,7 @@ struct Context {
     size_t stage_bytes = 0;
     // copy streams and events of the pipelined host-buffer mirror (created on first use)
     cudaStream_t h2d = nullptr, d2h = nullptr;
-    static constexpr int kMaxChunks = 16;
+    static constexpr int kMaxChunks = 32;
     cudaEvent_t ev_start = nullptr, ev_a = nullptr;
     cudaEvent_t ev_in[kMaxChunks] = {}, ev_out[kMaxChunks] = {};
     // device copy of tensor maps for pointer-array batches

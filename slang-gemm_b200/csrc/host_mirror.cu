@@ -197,8 +197,7 @@ extern "C" gs_status gs_host_gemm_ex(gs_handle h, const gs_ex_desc *d) {
     const size_t align = batch > 1 ? 1 : 256;
     const size_t total_bytes = a_bytes + b_bytes + c_bytes * (upload_c ? 2 : 1);
     size_t chunks = total_bytes / (32u << 20);
-    chunks = std::max<size_t>(1, std::min<size_t>({chunks, static_cast<size_t>(gs::Context::kMaxChunks),
-                                                   (units + align - 1) / align}));
+    chunks = std::max<size_t>(1, std::min<size_t>({chunks, static_cast<size_t>(16), (units + align - 1) / align}));
     // Only a contiguous Y column block can be uploaded per chunk (op N); otherwise Y goes first, whole.
     const bool y_chunked = batch == 1 && opy == GS_OP_N;
     cudaStream_t s = ctx.stream;
@@ -208,13 +207,84 @@ extern "C" gs_status gs_host_gemm_ex(gs_handle h, const gs_ex_desc *d) {
     if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_start, s);  // work already queued on the handle's stream
     if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx.h2d, ctx.ev_start, 0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx.d2h, ctx.ev_start, 0);
-    if (batch == 1) {
+
+    // Large single GEMM with X and Y both op N: 2-D pipeline. The first block
+    // of C needs only one row block of X and one column block of Y, instead of
+    // all of X, so downloads start after 1/R + 1/Q of the operand bytes. X row
+    // blocks and Y column blocks are uploaded alternately; after each upload
+    // the C blocks it completes are computed and downloaded (pitched copies).
+    const int RB = 4, QB = 4;
+    const bool two_d = batch == 1 && opx == GS_OP_N && opy == GS_OP_N && m >= 2048 && n >= 2048 && d->k >= 256 &&
+                       e == cudaSuccess;
+    if (two_d) {
+        size_t rcut[RB + 1], qcut[QB + 1];
+        for (int i = 0; i <= RB; ++i) rcut[i] = i == RB ? static_cast<size_t>(m) : (static_cast<size_t>(m) * i / RB) / 256 * 256;
+        for (int j = 0; j <= QB; ++j) qcut[j] = j == QB ? static_cast<size_t>(n) : (static_cast<size_t>(n) * j / QB) / 256 * 256;
+        const size_t ldxb = static_cast<size_t>(ldx) * esx, ldyb = static_cast<size_t>(ldy) * esy;
+        const size_t ldcb = d->ldc * esc;
+        int ev_n = 0;  // upload events used
+        int rows_up = 0, cols_up = 0;
+        auto issue_block = [&](int i, int j, cudaEvent_t ready) {
+            const size_t r0 = rcut[i], r1 = rcut[i + 1], c0 = qcut[j], c1 = qcut[j + 1];
+            const size_t coff = r0 * esc + c0 * ldcb;
+            cudaEvent_t in = ready;
+            // Only the block's own rows are written back, so padding between columns never
+            // needs the upload: C is uploaded only when it is read.
+            if (d->beta_re != 0.0 && e == cudaSuccess) {
+                e = cudaMemcpy2DAsync(dC + coff, ldcb, static_cast<const uint8_t *>(d->c) + coff, ldcb,
+                                      (r1 - r0) * esc, c1 - c0, cudaMemcpyHostToDevice, ctx.h2d);
+                if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_in[ev_n], ctx.h2d);
+                in = ctx.ev_in[ev_n++];
+            }
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(s, in, 0);
+            if (e != cudaSuccess) return;
+            st = gs_gemm_strided_batched_ex(h, GS_OP_N, GS_OP_N, static_cast<int>(r1 - r0), static_cast<int>(c1 - c0),
+                                            static_cast<int>(d->k), alpha, dX + r0 * esx, tx, ldx, 0,
+                                            dY + c0 * ldyb, ty, ldy, 0, beta, dC + coff, d->c_type,
+                                            static_cast<int>(d->ldc), 0, 1, d->compute_type, d->algo);
+            if (st != GS_STATUS_SUCCESS) return;
+            const int blk = i * QB + j;
+            e = cudaEventRecord(ctx.ev_out[blk], s);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx.d2h, ctx.ev_out[blk], 0);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(static_cast<uint8_t *>(d->c) + coff, ldcb, dC + coff, ldcb, (r1 - r0) * esc,
+                                      c1 - c0, cudaMemcpyDeviceToHost, ctx.d2h);
+        };
+        for (int step = 0; step < RB + QB && e == cudaSuccess && st == GS_STATUS_SUCCESS; ++step) {
+            const bool take_row = (step % 2 == 0 && rows_up < RB) || cols_up == QB;
+            if (take_row) {
+                const size_t r0 = rcut[rows_up], r1 = rcut[rows_up + 1];
+                e = cudaMemcpy2DAsync(dX + r0 * esx, ldxb, hX + r0 * esx, ldxb, (r1 - r0) * esx, d->k,
+                                      cudaMemcpyHostToDevice, ctx.h2d);
+                if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_in[ev_n], ctx.h2d);
+                cudaEvent_t ready = ctx.ev_in[ev_n++];
+                for (int j = 0; j < cols_up && e == cudaSuccess && st == GS_STATUS_SUCCESS; ++j)
+                    issue_block(rows_up, j, ready);
+                ++rows_up;
+            } else {
+                const size_t c0 = qcut[cols_up], c1 = qcut[cols_up + 1];
+                const size_t y0 = c0 * ldyb, y1 = ((c1 - 1) * ldy + d->k) * esy;
+                e = cudaMemcpyAsync(dY + y0, hY + y0, y1 - y0, cudaMemcpyHostToDevice, ctx.h2d);
+                if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_in[ev_n], ctx.h2d);
+                cudaEvent_t ready = ctx.ev_in[ev_n++];
+                for (int i = 0; i < rows_up && e == cudaSuccess && st == GS_STATUS_SUCCESS; ++i)
+                    issue_block(i, cols_up, ready);
+                ++cols_up;
+            }
+        }
+        if (st != GS_STATUS_SUCCESS) {
+            cudaStreamSynchronize(ctx.h2d);
+            cudaStreamSynchronize(ctx.d2h);
+            return st;
+        }
+    }
+    if (!two_d && batch == 1) {
         h2d(dX, hX, ext_x * esx);
         if (!y_chunked) h2d(dY, hY, ext_y * esy);
         if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_a, ctx.h2d);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ctx.ev_a, 0);
     }
-    for (size_t j = 0; j < chunks && e == cudaSuccess; ++j) {
+    for (size_t j = 0; !two_d && j < chunks && e == cudaSuccess; ++j) {
         size_t u0 = units * j / chunks, u1 = units * (j + 1) / chunks;
         if (j > 0) u0 = (u0 / align) * align;
         if (j + 1 < chunks) u1 = (u1 / align) * align;

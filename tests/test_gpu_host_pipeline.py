@@ -1,7 +1,8 @@
 """GPU parity of the pipelined host-buffer entry point gs_host_gemm_ex at sizes
-that make it cut C into several chunks (column blocks of one GEMM, or ranges
-of batch entries) with uploads, kernels and downloads overlapped on three
-streams. Checked against the oracle's exact per-element loop on sampled
+that make it cut C into several chunks (column blocks of one GEMM, ranges of
+batch entries, or — for large op N x op N GEMMs — a 4 x 4 grid of blocks fed by
+alternating row blocks of A and column blocks of B) with uploads, kernels and
+downloads overlapped on three streams. Checked against the oracle's exact per-element loop on sampled
 entries (plus whole first/last columns) and, for INT8, exact checksums.
 Bytes of C outside the matrix (padding between columns) must come back
 unchanged.
@@ -30,6 +31,8 @@ def _idx(layout, ld, r, c):
     (gs.R_16F, orc.ROW_MAJOR, 1, 0, 2048, 4096, 512, 1, 0.5, 8),    # row-major, beta != 0, padded ldc
     (gs.R_16F, orc.COL_MAJOR, 0, 0, 512, 512, 1024, 64, 0.0, 0),    # batch-range chunks
     (gs.R_8I, orc.COL_MAJOR, 1, 0, 256, 512, 256, 96, 1.0, 0),      # batched INT8, beta != 0
+    (gs.R_16F, orc.COL_MAJOR, 0, 0, 2304, 2560, 320, 1, 0.5, 8),    # 2-D blocks, beta != 0, padded ldc
+    (gs.R_16BF, orc.ROW_MAJOR, 0, 0, 2048, 3072, 256, 1, 0.0, 4),   # 2-D blocks (row-major), padding kept
 ])
 def test_pipelined_host_mirror(handle, dt, layout, op_a, op_b, m, n, k, batch, beta, ldc_pad):
     rng = np.random.default_rng(m + n + k + batch)
