@@ -40,6 +40,7 @@
 #include "gs_epilogue.cuh"
 #include "gs_internal.h"
 #include "gs_ptx.cuh"
+#include "gs_simt.cuh"
 
 namespace gs {
 namespace tc {
@@ -97,6 +98,7 @@ struct TcArgs {
     uint32_t skip_gen;
     int tma_store;               // epilogue writes C with TMA tensor stores (beta == 0, C TMA-addressable)
     int ab_evict_last;           // operand loads use the evict_last L2 policy
+    simt::SimtArgs fb;           // pointer-array batches: the CUDA-core fallback's view of the problem
     Epilogue ep;
     uint32_t *err;
 };
@@ -147,10 +149,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     grid_dep_wait();
     grid_dep_launch();
-    // Pointer-array batches whose pointers TMA cannot address are computed by
-    // the CUDA-core kernel launched after this one instead. Every CTA reads
-    // the same word, so both CTAs of a pair leave together.
-    if (args.skip_flag != nullptr && *args.skip_flag == args.skip_gen) return;
+    // Pointer-array batches whose pointers TMA cannot address: every CTA reads
+    // the same word and, instead of the tensor-core pipeline, runs the CUDA-core
+    // tile loop over the whole batch (both CTAs of a pair take the same path,
+    // before any cluster barrier or TMEM allocation).
+    if (args.skip_flag != nullptr && *args.skip_flag == args.skip_gen) {
+        simt::simt_tiles<IN, OUT>(args.fb, blockIdx.x, gridDim.x, smem);
+        return;
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -432,8 +438,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // a host-encoded template and patches the global address with
 // tensormap.replace, then makes the write visible to the tensor-map proxy.
 // A pointer that is not 16-byte aligned cannot be a TMA base address: the
-// builder then writes this call's tag `gen` into *misaligned, the tensor-core
-// kernel returns at once and the CUDA-core kernel computes the whole batch
+// builder then writes this call's tag `gen` into *misaligned and the
+// tensor-core kernel computes the whole batch with its CUDA-core fallback
 // instead (a word tagged by an earlier call never matches).
 __global__ void k_build_ptr_maps(const CUtensorMap tmpl_a, const CUtensorMap tmpl_b, const void *const *a_arr,
                                  const void *const *b_arr, CUtensorMap *maps_a, CUtensorMap *maps_b, int batch,
@@ -712,10 +718,8 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     args.c_arr = c_arr;
     args.skip_flag = misaligned;
     args.skip_gen = gen;
-    e = dispatch_shape(shape, ctx, d, ta, tb, tcm, args);
-    if (e != cudaSuccess) return e;
-    // Runs only when the builder tagged the word with this call's value.
-    return launch_simt_if_flag(ctx, d, a_arr, b_arr, c_arr, misaligned, gen);
+    args.fb = simt::make_args(d, a_arr, b_arr, c_arr);
+    return dispatch_shape(shape, ctx, d, ta, tb, tcm, args);
 }
 
 }  // namespace gs

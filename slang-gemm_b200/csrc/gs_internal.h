@@ -118,9 +118,6 @@ cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *
 cudaError_t launch_simt(Context &ctx, const GemmDesc &d, const void *const *a_arr,
                         const void *const *b_arr, void *const *c_arr);
 cudaError_t launch_scale(Context &ctx, const GemmDesc &d, void *const *c_arr);
-// CUDA-core pointer-array GEMM that does its work only when *flag == gen.
-cudaError_t launch_simt_if_flag(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
-                                void *const *c_arr, const uint32_t *flag, uint32_t gen);
 
 // Tensor-map encoder obtained from the driver at run time.
 bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t dim0,

@@ -17,7 +17,7 @@ from gpu_util import (NP_OF, assert_parity, make_c, make_input, to_dev, to_host)
 
 pytestmark = pytest.mark.gpu
 
-N_CASES = 96
+N_CASES = 256
 OUTS = {gs.R_16F: [gs.R_32F, gs.R_32F, gs.R_16F], gs.R_16BF: [gs.R_32F, gs.R_32F, gs.R_16BF], gs.R_8I: [gs.R_32I],
         gs.R_32F: [gs.R_32F]}
 COMPUTES = {(gs.R_16F, gs.R_32F): [gs.COMPUTE_32F, gs.COMPUTE_32F_FAST_16F],
