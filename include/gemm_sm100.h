@@ -221,6 +221,29 @@ typedef struct gs_ex_desc {
  * Device staging buffers are owned and reused by the handle. */
 gs_status gs_host_gemm_ex(gs_handle handle, const gs_ex_desc *desc);
 
+/* Mirrors PointerBatchedExDesc (src/gemm.zig:263-284): per-entry HOST byte
+ * buffers with their lengths; counts must agree (else InvalidBatchCount). */
+typedef struct gs_ptr_batched_desc {
+    int op_a, op_b;
+    size_t m, n, k;
+    double alpha_re, alpha_im;
+    const void *const *a; const size_t *a_lens; size_t a_count; int a_type; size_t lda;
+    const void *const *b; const size_t *b_lens; size_t b_count; int b_type; size_t ldb;
+    double beta_re, beta_im;
+    void *const *c; const size_t *c_lens; size_t c_count; int c_type; size_t ldc;
+    int compute_type;
+    int layout;
+    int algo;
+} gs_ptr_batched_desc;
+
+/* Drop-in for gemm.gemmBatchedEx (src/gemm.zig:636-663) over host buffers:
+ * the entries' A, B (and C when read) are packed into the handle's device
+ * staging, computed by one strided-batched call and copied back. Like the
+ * reference's entry-by-entry loop, when entry i fails validation the entries
+ * before it are still computed and written back, and the call returns
+ * GS_STATUS_INVALID_VALUE; entry i and later are untouched. Synchronous. */
+gs_status gs_host_gemm_batched_ex(gs_handle handle, const gs_ptr_batched_desc *desc);
+
 /* ---------------------------------------------------------------------- */
 /* Multi-GPU sharding plan (pure host logic)                               */
 /* ---------------------------------------------------------------------- */

@@ -47,6 +47,51 @@ gs_status check_len(size_t len, size_t es, size_t ext, size_t stride, size_t bat
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// f32 -> f16 bits, round to nearest even (finite, normal-range values; alpha/beta of COMPUTE_16F).
+uint16_t f32_to_f16_rne(float v) {
+    uint32_t x;
+    std::memcpy(&x, &v, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const int e = static_cast<int>((x >> 23) & 0xffu) - 127 + 15;
+    const uint32_t man = x & 0x7fffffu;
+    if (v == 0.0f) return static_cast<uint16_t>(sign);
+    if (e >= 31) return static_cast<uint16_t>(sign | 0x7c00u);
+    if (e <= 0) return static_cast<uint16_t>(sign);
+    uint32_t val = (static_cast<uint32_t>(e) << 10) | (man >> 13);
+    const uint32_t rem = man & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (val & 1u))) val++;
+    return static_cast<uint16_t>(sign | val);
+}
+
+// alpha / beta in the compute type's host representation: float for 32F*,
+// int32 for 32I* (integral values only), f16 bits for 16F*.
+struct HostScalars {
+    float f[2];
+    int32_t i[2];
+    uint16_t h[2];
+    const void *alpha = nullptr, *beta = nullptr;
+    bool set(int compute, double a, double b) {
+        f[0] = static_cast<float>(a);
+        f[1] = static_cast<float>(b);
+        alpha = &f[0];
+        beta = &f[1];
+        if (compute == GS_COMPUTE_32I || compute == GS_COMPUTE_32I_PEDANTIC) {
+            if (a != std::floor(a) || b != std::floor(b) || std::fabs(a) > 2147483647.0 || std::fabs(b) > 2147483647.0)
+                return false;
+            i[0] = static_cast<int32_t>(a);
+            i[1] = static_cast<int32_t>(b);
+            alpha = &i[0];
+            beta = &i[1];
+        } else if (compute == GS_COMPUTE_16F || compute == GS_COMPUTE_16F_PEDANTIC) {
+            h[0] = f32_to_f16_rne(f[0]);
+            h[1] = f32_to_f16_rne(f[1]);
+            alpha = &h[0];
+            beta = &h[1];
+        }
+        return true;
+    }
+};
+
 }  // namespace
 
 extern "C" gs_status gs_gemm_strided_batched_ex(gs_handle, int, int, int, int, int, const void *, const void *, int,
@@ -93,44 +138,12 @@ extern "C" gs_status gs_host_gemm_ex(gs_handle h, const gs_ex_desc *d) {
         return GS_STATUS_NOT_SUPPORTED;
     }
 
-    // alpha / beta in the compute type's host representation.
-    float af = static_cast<float>(d->alpha_re), bf = static_cast<float>(d->beta_re);
-    int32_t ai = 0, bi = 0;
-    uint16_t ah = 0, bh = 0;
-    const void *alpha = &af, *beta = &bf;
-    const bool int_compute = d->compute_type == GS_COMPUTE_32I || d->compute_type == GS_COMPUTE_32I_PEDANTIC;
-    const bool half_compute = d->compute_type == GS_COMPUTE_16F || d->compute_type == GS_COMPUTE_16F_PEDANTIC;
-    if (int_compute) {
-        if (d->alpha_re != std::floor(d->alpha_re) || d->beta_re != std::floor(d->beta_re) ||
-            std::fabs(d->alpha_re) > 2147483647.0 || std::fabs(d->beta_re) > 2147483647.0) {
-            ctx.last_error = "32I compute needs integral alpha/beta";
-            return GS_STATUS_NOT_SUPPORTED;
-        }
-        ai = static_cast<int32_t>(d->alpha_re);
-        bi = static_cast<int32_t>(d->beta_re);
-        alpha = &ai;
-        beta = &bi;
-    } else if (half_compute) {
-        // f32 -> f16 bits, round to nearest even (finite, normal-range values).
-        auto to_half = [](float v) -> uint16_t {
-            uint32_t x;
-            std::memcpy(&x, &v, 4);
-            const uint32_t sign = (x >> 16) & 0x8000u;
-            const int e = static_cast<int>((x >> 23) & 0xffu) - 127 + 15;
-            const uint32_t man = x & 0x7fffffu;
-            if (v == 0.0f) return static_cast<uint16_t>(sign);
-            if (e >= 31) return static_cast<uint16_t>(sign | 0x7c00u);
-            if (e <= 0) return static_cast<uint16_t>(sign);
-            uint32_t val = (static_cast<uint32_t>(e) << 10) | (man >> 13);
-            const uint32_t rem = man & 0x1fffu;
-            if (rem > 0x1000u || (rem == 0x1000u && (val & 1u))) val++;
-            return static_cast<uint16_t>(sign | val);
-        };
-        ah = to_half(af);
-        bh = to_half(bf);
-        alpha = &ah;
-        beta = &bh;
+    HostScalars sc_ab;
+    if (!sc_ab.set(d->compute_type, d->alpha_re, d->beta_re)) {
+        ctx.last_error = "32I compute needs integral alpha/beta";
+        return GS_STATUS_NOT_SUPPORTED;
     }
+    const void *alpha = sc_ab.alpha, *beta = sc_ab.beta;
 
     // Stage A, B, C in one device region.
     const size_t a_bytes = ((d->batch_count - 1) * sa + a_ext) * esa;
@@ -345,4 +358,126 @@ extern "C" gs_status gs_host_gemm_ex(gs_handle h, const gs_ex_desc *d) {
         return GS_STATUS_EXECUTION_FAILED;
     }
     return GS_STATUS_SUCCESS;
+}
+
+// gemm.gemmBatchedEx over host buffers (src/gemm.zig:636-663). Each entry is an
+// ExDesc with batch_count 1 (stride = one extent); the valid prefix of entries
+// is packed into the staging region at extent strides and computed by one
+// strided-batched call.
+extern "C" gs_status gs_host_gemm_batched_ex(gs_handle h, const gs_ptr_batched_desc *d) {
+    if (!h) return GS_STATUS_NOT_INITIALIZED;
+    gs::Context &ctx = h->ctx;
+    if (!d) return GS_STATUS_INVALID_VALUE;
+    if (d->a_count != d->b_count || d->a_count != d->c_count) {
+        ctx.last_error = "pointer counts differ (InvalidBatchCount)";
+        return GS_STATUS_INVALID_VALUE;
+    }
+    const size_t count = d->a_count;
+    if (count == 0) return GS_STATUS_SUCCESS;
+    if (!d->a || !d->b || !d->c || !d->a_lens || !d->b_lens || !d->c_lens) {
+        ctx.last_error = "null pointer array";
+        return GS_STATUS_INVALID_VALUE;
+    }
+    if (d->layout != GS_LAYOUT_ROW_MAJOR && d->layout != GS_LAYOUT_COL_MAJOR) {
+        ctx.last_error = "invalid layout";
+        return GS_STATUS_INVALID_VALUE;
+    }
+    const size_t esa = type_size(d->a_type), esb = type_size(d->b_type), esc = type_size(d->c_type);
+    if (!esa || !esb || !esc) {
+        ctx.last_error = "unsupported data type";
+        return GS_STATUS_NOT_SUPPORTED;
+    }
+    const bool ta = d->op_a != GS_OP_N, tb = d->op_b != GS_OP_N;
+    const size_t a_ext = extent(d->layout, d->lda, ta ? d->k : d->m, ta ? d->m : d->k);
+    const size_t b_ext = extent(d->layout, d->ldb, tb ? d->n : d->k, tb ? d->k : d->n);
+    const size_t c_ext = extent(d->layout, d->ldc, d->m, d->n);
+    // The reference validates entry by entry inside its loop: find the valid prefix.
+    size_t valid = 0;
+    std::string why;
+    gs_status bad = GS_STATUS_SUCCESS;
+    for (; valid < count; ++valid) {
+        std::string w;
+        gs_status st;
+        if ((st = check_len(d->a_lens[valid], esa, a_ext, a_ext, 1, "a", &w)) != GS_STATUS_SUCCESS ||
+            (st = check_len(d->b_lens[valid], esb, b_ext, b_ext, 1, "b", &w)) != GS_STATUS_SUCCESS ||
+            (st = check_len(d->c_lens[valid], esc, c_ext, c_ext, 1, "c", &w)) != GS_STATUS_SUCCESS) {
+            bad = st;
+            why = "entry " + std::to_string(valid) + ": " + w;
+            break;
+        }
+    }
+    gs_status st = GS_STATUS_SUCCESS;
+    if (valid > 0 && d->m != 0 && d->n != 0) {
+        const size_t lim = 0x7fffffff;
+        if (d->m > lim || d->n > lim || d->k > lim || d->lda > lim || d->ldb > lim || d->ldc > lim || valid > lim) {
+            ctx.last_error = "dimension exceeds the 32-bit device API";
+            return GS_STATUS_NOT_SUPPORTED;
+        }
+        HostScalars sc_ab;
+        if (!sc_ab.set(d->compute_type, d->alpha_re, d->beta_re)) {
+            ctx.last_error = "32I compute needs integral alpha/beta";
+            return GS_STATUS_NOT_SUPPORTED;
+        }
+        // Packed staging: entry j of A at j * a_ext elements, and so on.
+        const size_t a_bytes = valid * a_ext * esa, b_bytes = valid * b_ext * esb, c_bytes = valid * c_ext * esc;
+        const size_t off_b = round_up(a_bytes, 256), off_c = off_b + round_up(b_bytes, 256);
+        const size_t need = off_c + round_up(c_bytes, 256);
+        if (ctx.stage_bytes < need) {
+            if (ctx.stage) cudaFree(ctx.stage);
+            ctx.stage = nullptr;
+            ctx.stage_bytes = 0;
+            if (cudaMalloc(&ctx.stage, need) != cudaSuccess) {
+                cudaGetLastError();
+                ctx.last_error = "device staging allocation failed";
+                return GS_STATUS_ALLOC_FAILED;
+            }
+            ctx.stage_bytes = need;
+        }
+        uint8_t *dA = static_cast<uint8_t *>(ctx.stage), *dB = dA + off_b, *dC = dA + off_c;
+        // C is uploaded when it is read, or when padding between its columns
+        // (rows) would otherwise come back from the device as garbage.
+        const bool c_dense = d->layout == GS_LAYOUT_COL_MAJOR ? d->ldc == d->m : d->ldc == d->n;
+        const bool upload_c = d->beta_re != 0.0 || !c_dense;
+        cudaStream_t s = ctx.stream;
+        cudaError_t e = cudaSuccess;
+        for (size_t j = 0; j < valid && e == cudaSuccess; ++j) {
+            if (a_ext) e = cudaMemcpyAsync(dA + j * a_ext * esa, d->a[j], a_ext * esa, cudaMemcpyHostToDevice, s);
+            if (e == cudaSuccess && b_ext)
+                e = cudaMemcpyAsync(dB + j * b_ext * esb, d->b[j], b_ext * esb, cudaMemcpyHostToDevice, s);
+            if (e == cudaSuccess && upload_c && c_ext)
+                e = cudaMemcpyAsync(dC + j * c_ext * esc, d->c[j], c_ext * esc, cudaMemcpyHostToDevice, s);
+        }
+        if (e != cudaSuccess) {
+            cudaStreamSynchronize(s);
+            ctx.last_error = std::string("host-buffer upload: ") + cudaGetErrorString(e);
+            return GS_STATUS_EXECUTION_FAILED;
+        }
+        const bool rm = d->layout == GS_LAYOUT_ROW_MAJOR;
+        const int m = static_cast<int>(rm ? d->n : d->m), n = static_cast<int>(rm ? d->m : d->n);
+        st = gs_gemm_strided_batched_ex(h, rm ? d->op_b : d->op_a, rm ? d->op_a : d->op_b, m, n, static_cast<int>(d->k),
+                                        sc_ab.alpha, rm ? dB : dA, rm ? d->b_type : d->a_type,
+                                        static_cast<int>(rm ? d->ldb : d->lda),
+                                        static_cast<long long>(rm ? b_ext : a_ext), rm ? dA : dB,
+                                        rm ? d->a_type : d->b_type, static_cast<int>(rm ? d->lda : d->ldb),
+                                        static_cast<long long>(rm ? a_ext : b_ext), sc_ab.beta, dC, d->c_type,
+                                        static_cast<int>(d->ldc), static_cast<long long>(c_ext),
+                                        static_cast<int>(valid), d->compute_type, d->algo);
+        if (st == GS_STATUS_SUCCESS) {
+            for (size_t j = 0; j < valid && e == cudaSuccess; ++j)
+                if (c_ext) e = cudaMemcpyAsync(d->c[j], dC + j * c_ext * esc, c_ext * esc, cudaMemcpyDeviceToHost, s);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess) {
+                ctx.last_error = std::string("host-buffer download: ") + cudaGetErrorString(e);
+                return GS_STATUS_EXECUTION_FAILED;
+            }
+        } else {
+            cudaStreamSynchronize(s);
+            return st;
+        }
+    }
+    if (bad != GS_STATUS_SUCCESS) {
+        ctx.last_error = why;
+        return bad;
+    }
+    return st;
 }

@@ -81,6 +81,24 @@ class ExDesc(ctypes.Structure):
     ]
 
 
+class PtrBatchedDesc(ctypes.Structure):
+    """gs_ptr_batched_desc: mirrors PointerBatchedExDesc (src/gemm.zig:263-284)."""
+
+    _fields_ = [
+        ("op_a", ctypes.c_int), ("op_b", ctypes.c_int),
+        ("m", ctypes.c_size_t), ("n", ctypes.c_size_t), ("k", ctypes.c_size_t),
+        ("alpha_re", ctypes.c_double), ("alpha_im", ctypes.c_double),
+        ("a", ctypes.POINTER(ctypes.c_void_p)), ("a_lens", ctypes.POINTER(ctypes.c_size_t)),
+        ("a_count", ctypes.c_size_t), ("a_type", ctypes.c_int), ("lda", ctypes.c_size_t),
+        ("b", ctypes.POINTER(ctypes.c_void_p)), ("b_lens", ctypes.POINTER(ctypes.c_size_t)),
+        ("b_count", ctypes.c_size_t), ("b_type", ctypes.c_int), ("ldb", ctypes.c_size_t),
+        ("beta_re", ctypes.c_double), ("beta_im", ctypes.c_double),
+        ("c", ctypes.POINTER(ctypes.c_void_p)), ("c_lens", ctypes.POINTER(ctypes.c_size_t)),
+        ("c_count", ctypes.c_size_t), ("c_type", ctypes.c_int), ("ldc", ctypes.c_size_t),
+        ("compute_type", ctypes.c_int), ("layout", ctypes.c_int), ("algo", ctypes.c_int),
+    ]
+
+
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
@@ -108,6 +126,7 @@ def _load() -> ctypes.CDLL:
         "gs_plan_gemm_strided_batched_ex": (st, [i, i, i, i, i, vp, i, i, ll, vp, i, i, ll, vp, i, i, ll, i, i,
                                                  ctypes.POINTER(u32)]),
         "gs_host_gemm_ex": (st, [vp, ctypes.POINTER(ExDesc)]),
+        "gs_host_gemm_batched_ex": (st, [vp, ctypes.POINTER(PtrBatchedDesc)]),
         "gs_plan_shards": (st, [ll, i, ll, ctypes.POINTER(ll)]),
         "gs_gemm_batched_ex_noalloc": (st, [vp, i, i, i, i, i, vp, vp, i, i, vp, i, i, vp, vp, i, i, i, i]),
         "gs_multi_create": (st, [ctypes.POINTER(vp), i, ctypes.POINTER(i)]),
@@ -330,6 +349,35 @@ class Handle:
         s = _lib.gs_host_gemm_ex(self._h, ctypes.byref(d))
         if check:
             self._check(s, "gs_host_gemm_ex")
+        return s
+
+    def host_gemm_batched_ex(self, op_a, op_b, m, n, k, alpha, a_list, a_type, lda, b_list, b_type, ldb, beta,
+                             c_list, c_type, ldc, compute, layout=LAYOUT_COL_MAJOR, algo=GEMM_DEFAULT,
+                             check=True) -> int:
+        """Mirror of gemm.gemmBatchedEx (src/gemm.zig:636-663): lists of host buffers
+        (numpy arrays or CPU tensors), one per entry; each c is updated in place."""
+        def bufs(xs):
+            ptrs, lens = [], []
+            for x in xs:
+                if hasattr(x, "data_ptr"):
+                    ptrs.append(x.data_ptr())
+                    lens.append(x.numel() * x.element_size())
+                else:
+                    ptrs.append(x.ctypes.data)
+                    lens.append(x.nbytes)
+            return ((ctypes.c_void_p * max(1, len(ptrs)))(*ptrs), (ctypes.c_size_t * max(1, len(lens)))(*lens),
+                    len(ptrs))
+
+        pa, la, na = bufs(a_list)
+        pb, lb, nb = bufs(b_list)
+        pc, lc, nc = bufs(c_list)
+        vpp = ctypes.POINTER(ctypes.c_void_p)
+        d = PtrBatchedDesc(op_a, op_b, m, n, k, float(alpha), 0.0, ctypes.cast(pa, vpp), la, na, a_type, lda,
+                           ctypes.cast(pb, vpp), lb, nb, b_type, ldb, float(beta), 0.0, ctypes.cast(pc, vpp), lc, nc,
+                           c_type, ldc, compute, layout, algo)
+        s = _lib.gs_host_gemm_batched_ex(self._h, ctypes.byref(d))
+        if check:
+            self._check(s, "gs_host_gemm_batched_ex")
         return s
 
 

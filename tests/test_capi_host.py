@@ -41,6 +41,8 @@ def test_null_handle_is_not_initialized():
     assert L.gs_gemm_ex(None, 0, 0, 4, 4, 4, ctypes.byref(one), ALIGNED, gs.R_16F, 4, ALIGNED, gs.R_16F, 4,
                         ctypes.byref(one), ALIGNED, gs.R_32F, 4, gs.COMPUTE_32F, -1) == gs.STATUS_NOT_INITIALIZED
     assert L.gs_set_stream(None, None) == gs.STATUS_NOT_INITIALIZED
+    assert L.gs_host_gemm_ex(None, None) == gs.STATUS_NOT_INITIALIZED
+    assert L.gs_host_gemm_batched_ex(None, None) == gs.STATUS_NOT_INITIALIZED
     assert L.gs_destroy(None) == gs.STATUS_NOT_INITIALIZED
 
 
