@@ -182,6 +182,10 @@ extern "C" gs_status gs_host_gemm_ex(gs_handle h, const gs_ex_desc *d) {
     const size_t esx = rm ? esb : esa, esy = rm ? esa : esb;
     const size_t ext_x = rm ? b_ext : a_ext, ext_y = rm ? a_ext : b_ext;
     const int ldx = static_cast<int>(rm ? d->ldb : d->lda), ldy = static_cast<int>(rm ? d->lda : d->ldb);
+    // src/gemm.zig never checks a leading dimension, and with k == 0 neither
+    // operand is read: any ld the device API accepts will do there.
+    const int ld_k0 = static_cast<int>(std::max<size_t>({1, d->m, d->n}));
+    const int ldx_dev = d->k == 0 ? ld_k0 : ldx, ldy_dev = d->k == 0 ? ld_k0 : ldy;
     const size_t sx = rm ? sb : sa, sy = rm ? sa : sb;
     const int tx = rm ? d->b_type : d->a_type, ty = rm ? d->a_type : d->b_type;
     const size_t batch = d->batch_count;
@@ -334,8 +338,8 @@ extern "C" gs_status gs_host_gemm_ex(gs_handle h, const gs_ex_desc *d) {
         if (e == cudaSuccess) e = cudaEventRecord(ctx.ev_in[j], ctx.h2d);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ctx.ev_in[j], 0);
         if (e != cudaSuccess) break;
-        st = gs_gemm_strided_batched_ex(h, opx, opy, m, nn, static_cast<int>(d->k), alpha, X, tx, ldx,
-                                        static_cast<long long>(sx), Y, ty, ldy, static_cast<long long>(sy), beta, C,
+        st = gs_gemm_strided_batched_ex(h, opx, opy, m, nn, static_cast<int>(d->k), alpha, X, tx, ldx_dev,
+                                        static_cast<long long>(sx), Y, ty, ldy_dev, static_cast<long long>(sy), beta, C,
                                         d->c_type, static_cast<int>(d->ldc), static_cast<long long>(sc), bb,
                                         d->compute_type, d->algo);
         if (st != GS_STATUS_SUCCESS) {
@@ -454,11 +458,14 @@ extern "C" gs_status gs_host_gemm_batched_ex(gs_handle h, const gs_ptr_batched_d
         }
         const bool rm = d->layout == GS_LAYOUT_ROW_MAJOR;
         const int m = static_cast<int>(rm ? d->n : d->m), n = static_cast<int>(rm ? d->m : d->n);
+        // With k == 0 neither operand is read (and src/gemm.zig checks no leading dimension).
+        const size_t ld_k0 = std::max<size_t>({1, d->m, d->n});
+        const size_t lda_dev = d->k == 0 ? ld_k0 : d->lda, ldb_dev = d->k == 0 ? ld_k0 : d->ldb;
         st = gs_gemm_strided_batched_ex(h, rm ? d->op_b : d->op_a, rm ? d->op_a : d->op_b, m, n, static_cast<int>(d->k),
                                         sc_ab.alpha, rm ? dB : dA, rm ? d->b_type : d->a_type,
-                                        static_cast<int>(rm ? d->ldb : d->lda),
+                                        static_cast<int>(rm ? ldb_dev : lda_dev),
                                         static_cast<long long>(rm ? b_ext : a_ext), rm ? dA : dB,
-                                        rm ? d->a_type : d->b_type, static_cast<int>(rm ? d->lda : d->ldb),
+                                        rm ? d->a_type : d->b_type, static_cast<int>(rm ? lda_dev : ldb_dev),
                                         static_cast<long long>(rm ? a_ext : b_ext), sc_ab.beta, dC, d->c_type,
                                         static_cast<int>(d->ldc), static_cast<long long>(c_ext),
                                         static_cast<int>(valid), d->compute_type, d->algo);

@@ -22,6 +22,15 @@
 // accesses. Operands stored K-contiguous (A op T, B op N) are transposed into
 // the [k][m] / [k][n] shared layout with scalar stores into rows padded by 4
 // floats (at most 2-way bank conflicts).
+//
+// Problems whose 64 x 64 grid cannot fill the SMs (512^3 gives 64 tiles) split
+// K across a thread-block cluster of S CTAs (S = 2, 4, 8): each CTA runs the
+// same tile over 1/S of the K steps, parks its partial tile in shared memory,
+// and after a cluster barrier CTA r sums slice r of the tile from all S
+// partials through distributed shared memory, in rank order (deterministic),
+// and applies alpha / beta. No workspace, no atomics, one launch.
+#include <cooperative_groups.h>
+
 #include "gs_epilogue.cuh"
 #include "gs_internal.h"
 
@@ -146,7 +155,25 @@ __device__ __forceinline__ void store_b(float *Bs, int lds, int c, const float4 
     }
 }
 
-template <int TA, int TB, class T>
+// alpha * v then + beta * C, four consecutive rows of one column (16-byte aligned).
+__device__ __forceinline__ void store4(float *p, float4 v, const Epilogue &ep) {
+    if (!ep.identity) {
+        v.x = __fmul_rn(ep.alpha_f, v.x); v.y = __fmul_rn(ep.alpha_f, v.y);
+        v.z = __fmul_rn(ep.alpha_f, v.z); v.w = __fmul_rn(ep.alpha_f, v.w);
+    }
+    if (!ep.beta_zero) {
+        const float4 o = *reinterpret_cast<const float4 *>(p);
+        v.x = __fadd_rn(v.x, __fmul_rn(ep.beta_f, o.x));
+        v.y = __fadd_rn(v.y, __fmul_rn(ep.beta_f, o.y));
+        v.z = __fadd_rn(v.z, __fmul_rn(ep.beta_f, o.z));
+        v.w = __fadd_rn(v.w, __fmul_rn(ep.beta_f, o.w));
+    }
+    *reinterpret_cast<float4 *>(p) = v;
+}
+
+// S = 1: one CTA per tile, grid.x = M tiles. S > 1: clusters of S CTAs along x
+// share a tile (grid.x = M tiles * S), CTA rank r runs K steps [r*ceil(kt/S), ...).
+template <int TA, int TB, class T, int S>
 __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaArgs a) {
     constexpr int BM = T::BM, BN = T::BN, BK = T::BK, RM = T::RM, RN = T::RN;
     constexpr int LDA_S = BM + (TA == 1 ? 4 : 0);   // padded when filled by transposing stores
@@ -157,9 +184,13 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
     grid_dep_launch();
     const int tid = threadIdx.x;
     const int tx = tid % T::TX, ty = tid / T::TX;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int rank = S > 1 ? static_cast<int>(blockIdx.x % S) : 0;
+    const int m0 = static_cast<int>(blockIdx.x / S) * BM, n0 = blockIdx.y * BN;
     const bool full_m = m0 + BM <= a.m, full_n = n0 + BN <= a.n;
-    const int ktiles = (a.k + BK - 1) / BK;
+    const int kt_all = (a.k + BK - 1) / BK;
+    const int kt_per = (kt_all + S - 1) / S;
+    const int kt0 = rank * kt_per < kt_all ? rank * kt_per : kt_all;
+    const int kt1 = kt0 + kt_per < kt_all ? kt0 + kt_per : kt_all;
 
     for (int b = blockIdx.z; b < a.batch; b += gridDim.z) {
         const float *A = a.a_arr ? a.a_arr[b] : a.A + static_cast<size_t>(b) * a.stride_a;
@@ -177,12 +208,13 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
             for (int j = 0; j < 4 * RN; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
 
         float4 ra[T::CH_A], rb[T::CH_B];
-        {
-            const bool fk = BK <= a.k;
+        if (kt0 < kt1) {
+            const int k0 = kt0 * BK;
+            const bool fk = k0 + BK <= a.k;
 #pragma unroll
-            for (int i = 0; i < T::CH_A; ++i) load_a<TA, T>(a, A, m0, 0, tid + i * T::THREADS, va && full_m && fk, ra[i]);
+            for (int i = 0; i < T::CH_A; ++i) load_a<TA, T>(a, A, m0, k0, tid + i * T::THREADS, va && full_m && fk, ra[i]);
 #pragma unroll
-            for (int i = 0; i < T::CH_B; ++i) load_b<TB, T>(a, B, n0, 0, tid + i * T::THREADS, vb && full_n && fk, rb[i]);
+            for (int i = 0; i < T::CH_B; ++i) load_b<TB, T>(a, B, n0, k0, tid + i * T::THREADS, vb && full_n && fk, rb[i]);
 #pragma unroll
             for (int i = 0; i < T::CH_A; ++i) store_a<TA, T>(As[0], LDA_S, tid + i * T::THREADS, ra[i]);
 #pragma unroll
@@ -190,9 +222,9 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
         }
         __syncthreads();
 
-        for (int kt = 0; kt < ktiles; ++kt) {
-            const int cur = kt & 1;
-            const bool more = kt + 1 < ktiles;
+        for (int kt = kt0; kt < kt1; ++kt) {
+            const int cur = (kt - kt0) & 1;
+            const bool more = kt + 1 < kt1;
             if (more) {
                 const int k0 = (kt + 1) * BK;
                 const bool fk = k0 + BK <= a.k;
@@ -245,6 +277,44 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
             __syncthreads();
         }
 
+        if constexpr (S > 1) {
+            // Partial tile, column-major (BM floats per column), then the cluster reduction.
+            __shared__ __align__(16) float P[BM * BN];
+            namespace cg = cooperative_groups;
+            cg::cluster_group cluster = cg::this_cluster();
+#pragma unroll
+            for (int j = 0; j < 4 * RN; ++j) {
+                const int ln = (j / 4) * (BN / RN) + ty * 4 + (j & 3);
+#pragma unroll
+                for (int r = 0; r < RM; ++r)
+                    *reinterpret_cast<float4 *>(&P[ln * BM + r * (BM / RM) + tx * 4]) =
+                        make_float4(acc2[2 * r][j].x, acc2[2 * r][j].y, acc2[2 * r + 1][j].x, acc2[2 * r + 1][j].y);
+            }
+            cluster.sync();
+            const float *parts[S];
+#pragma unroll
+            for (int q = 0; q < S; ++q) parts[q] = cluster.map_shared_rank(P, q);
+            constexpr int SLICE = BM * BN / S;   // floats of the tile this CTA finishes
+            const bool fast_c = vc && full_m && full_n;
+            for (int e = rank * SLICE + tid * 4; e < (rank + 1) * SLICE; e += T::THREADS * 4) {
+                float4 v = *reinterpret_cast<const float4 *>(parts[0] + e);
+#pragma unroll
+                for (int q = 1; q < S; ++q) {
+                    const float4 w = *reinterpret_cast<const float4 *>(parts[q] + e);
+                    v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+                }
+                const int gm = m0 + e % BM, gn = n0 + e / BM;
+                if (fast_c) {
+                    store4(C + static_cast<size_t>(gn) * a.ldc + gm, v, a.ep);
+                } else if (gn < a.n) {
+                    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (gm + i < a.m) store_facc<OUT_F32>(C, static_cast<size_t>(gn) * a.ldc + gm + i, vv[i], a.ep);
+                }
+            }
+            cluster.sync();   // partials stay readable until every CTA of the cluster is done
+        } else {
         float acc[4 * RM][4 * RN];
 #pragma unroll
         for (int i = 0; i < 2 * RM; ++i)
@@ -264,19 +334,8 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
                 const int gm = m0 + r * (BM / RM) + tx * 4;
                 float *p = C + static_cast<size_t>(gn) * a.ldc + gm;
                 if (fast_c) {
-                    float4 v = make_float4(acc[r * 4 + 0][j], acc[r * 4 + 1][j], acc[r * 4 + 2][j], acc[r * 4 + 3][j]);
-                    if (!a.ep.identity) {
-                        v.x = __fmul_rn(a.ep.alpha_f, v.x); v.y = __fmul_rn(a.ep.alpha_f, v.y);
-                        v.z = __fmul_rn(a.ep.alpha_f, v.z); v.w = __fmul_rn(a.ep.alpha_f, v.w);
-                    }
-                    if (!a.ep.beta_zero) {
-                        const float4 o = *reinterpret_cast<const float4 *>(p);
-                        v.x = __fadd_rn(v.x, __fmul_rn(a.ep.beta_f, o.x));
-                        v.y = __fadd_rn(v.y, __fmul_rn(a.ep.beta_f, o.y));
-                        v.z = __fadd_rn(v.z, __fmul_rn(a.ep.beta_f, o.z));
-                        v.w = __fadd_rn(v.w, __fmul_rn(a.ep.beta_f, o.w));
-                    }
-                    *reinterpret_cast<float4 *>(p) = v;
+                    store4(p, make_float4(acc[r * 4 + 0][j], acc[r * 4 + 1][j], acc[r * 4 + 2][j], acc[r * 4 + 3][j]),
+                           a.ep);
                 } else if (gn < a.n) {
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
@@ -284,23 +343,24 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
                 }
             }
         }
+        }
     }
 }
 
-template <int TA, int TB, class T>
+template <int TA, int TB, class T, int S>
 static cudaError_t go(Context &ctx, const FfmaArgs &a) {
-    dim3 grid((a.m + T::BM - 1) / T::BM, (a.n + T::BN - 1) / T::BN, a.batch < 65535 ? a.batch : 65535);
-    const cudaError_t e = launch_pdl(k_sgemm_ffma<TA, TB, T>, grid, dim3(T::THREADS), 0, ctx.stream, 1, a);
+    dim3 grid((a.m + T::BM - 1) / T::BM * S, (a.n + T::BN - 1) / T::BN, a.batch < 65535 ? a.batch : 65535);
+    const cudaError_t e = launch_pdl(k_sgemm_ffma<TA, TB, T, S>, grid, dim3(T::THREADS), 0, ctx.stream, S, a);
     ctx.launches++;
     return e;
 }
 
-template <class T>
+template <class T, int S = 1>
 static cudaError_t go_ops(Context &ctx, const GemmDesc &d, const FfmaArgs &a) {
-    if (!d.trans_a && !d.trans_b) return go<0, 0, T>(ctx, a);
-    if (!d.trans_a && d.trans_b) return go<0, 1, T>(ctx, a);
-    if (d.trans_a && !d.trans_b) return go<1, 0, T>(ctx, a);
-    return go<1, 1, T>(ctx, a);
+    if (!d.trans_a && !d.trans_b) return go<0, 0, T, S>(ctx, a);
+    if (!d.trans_a && d.trans_b) return go<0, 1, T, S>(ctx, a);
+    if (d.trans_a && !d.trans_b) return go<1, 0, T, S>(ctx, a);
+    return go<1, 1, T, S>(ctx, a);
 }
 
 template <class T>
@@ -311,7 +371,10 @@ static long long ctas(const GemmDesc &d) {
 }  // namespace ffma
 
 // Tile choice: the largest tile whose grid still gives every SM at least one
-// CTA; grids of the smallest tile for problems too small to fill the GPU.
+// CTA; below that the 64 x 64 tile with K split over a cluster of S CTAs
+// (S the power of two, at most 8, that brings the grid to the SM count while
+// every CTA keeps at least two K steps); the 32 x 32 tile when K is too short
+// to split.
 // a_arr/b_arr/c_arr: device arrays of per-entry pointers (pointer-array
 // batches), or nullptr for the strided layout of `d`.
 cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
@@ -335,7 +398,14 @@ cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *
     a.ep = d.ep;
     const long long sms = ctx.sm_count > 0 ? ctx.sm_count : 148;
     if (ctas<TileL>(d) >= sms) return go_ops<TileL>(ctx, d, a);
-    if (ctas<TileM>(d) >= sms) return go_ops<TileM>(ctx, d, a);
+    const long long cm = ctas<TileM>(d);
+    if (cm >= sms) return go_ops<TileM>(ctx, d, a);
+    const int ksteps = (d.k + TileM::BK - 1) / TileM::BK;
+    int split = 1;
+    while (split < 8 && cm * split < sms && ksteps >= 4 * split) split *= 2;
+    if (split == 8) return go_ops<TileM, 8>(ctx, d, a);
+    if (split == 4) return go_ops<TileM, 4>(ctx, d, a);
+    if (split == 2) return go_ops<TileM, 2>(ctx, d, a);
     return go_ops<TileS>(ctx, d, a);
 }
 

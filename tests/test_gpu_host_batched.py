@@ -112,3 +112,18 @@ def test_host_batched_short_entry_keeps_prefix(handle, bad):
 def test_host_batched_empty_lists(handle):
     assert handle.host_gemm_batched_ex(0, 0, 8, 8, 8, 1.0, [], gs.R_16F, 8, [], gs.R_16F, 8, 0.0, [], gs.R_32F, 8,
                                        gs.COMPUTE_32F, check=False) == gs.STATUS_SUCCESS
+
+
+def test_host_gemm_ex_k0_ignores_leading_dimensions(handle):
+    """src/gemm.zig checks no leading dimension; with k == 0 nothing but C is touched, so ld 0 is accepted."""
+    rng = np.random.default_rng(3)
+    m, n = 64, 48
+    a = make_input(rng, 1, gs.R_16F)
+    b = make_input(rng, 1, gs.R_16F)
+    c0 = make_c(rng, m * n, gs.R_32F)
+    got = c0.copy()
+    handle.host_gemm_ex(0, 0, m, n, 0, 2.0, a, gs.R_16F, 0, b, gs.R_16F, 0, 0.5, got, gs.R_32F, m, gs.COMPUTE_32F)
+    ref = c0.copy()
+    assert orc.gemm_ex(0, 0, m, n, 0, 2.0, a, gs.R_16F, 0, b, gs.R_16F, 0, 0.5, ref, gs.R_32F, m,
+                       compute_type=gs.COMPUTE_32F) == orc.OK
+    np.testing.assert_array_equal(got, ref)

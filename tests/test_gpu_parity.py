@@ -372,3 +372,21 @@ def test_fp32_fast_tf32_runs_exact_ffma(handle, op_a, op_b):
 def test_sgemm_tile_sizes(handle, m, n, k, op_a, op_b):
     """The FFMA kernel's three CTA tiles (32x32, 64x64, 128x128, chosen by grid size) on ragged shapes."""
     run_case(handle, gs.R_32F, op_a, op_b, m, n, k, alpha=1.5, beta=0.5, seed=m + n + k, expect_kernel=gs.KERNEL_FFMA)
+
+
+@pytest.mark.parametrize("m,n,k,batch,pad", [
+    (512, 512, 512, 1, (0, 0, 0)),      # 64 tiles: K split over clusters of 4
+    (64, 64, 4096, 1, (0, 0, 0)),       # one tile: clusters of 8
+    (100, 300, 1000, 1, (0, 0, 0)),     # ragged M, N and K (62.5 K steps over 8 CTAs)
+    (64, 64, 528, 1, (0, 0, 0)),        # 33 K steps over 8 CTAs: the last CTA has none
+    (64, 64, 70, 1, (0, 0, 0)),         # 5 K steps: clusters of 2
+    (200, 200, 512, 2, (0, 0, 0)),      # batched, clusters of 8
+    (96, 72, 260, 1, (1, 3, 2)),        # leading dimensions not multiples of 4: scalar loads and stores
+])
+@pytest.mark.parametrize("op_a,op_b", [(0, 0), (1, 1), (1, 0)])
+def test_sgemm_cluster_split_k(handle, m, n, k, batch, pad, op_a, op_b):
+    """Small FP32 problems split K across a thread-block cluster and reduce the partial tiles through
+    distributed shared memory; the result must match the oracle to the FP32 tolerance, with alpha and beta
+    applied once, and bytes outside C unchanged."""
+    run_case(handle, gs.R_32F, op_a, op_b, m, n, k, alpha=1.5, beta=-0.5, pad=pad, batch=batch, seed=m * n + k,
+             expect_kernel=gs.KERNEL_FFMA)
