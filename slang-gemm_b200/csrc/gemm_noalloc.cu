@@ -25,8 +25,8 @@
 namespace {
 
 constexpr int kMaxBatch = GS_NOALLOC_MAX_BATCH;
-constexpr size_t kMapBytes = 2ull * kMaxBatch * sizeof(CUtensorMap);  // A maps, then B maps
-constexpr size_t kWordBytes = 256;                                     // [0] error word, [1] misaligned flag
+constexpr size_t kMapBytes = 3ull * kMaxBatch * sizeof(CUtensorMap);  // A maps, B maps, C maps
+constexpr size_t kWordBytes = 256;                                     // [0] error word, [1] / [2] misaligned flags
 constexpr size_t kScratchBytes = kMapBytes + kWordBytes;
 
 // Device scratch of the no-allocation path. In host code this name is only a
@@ -108,7 +108,7 @@ extern "C" gs_status gs_gemm_batched_ex_noalloc(void *stream, int transa, int tr
     ctx.tmap_buf = slot->scratch;
     ctx.tmap_bytes = kMapBytes;
     ctx.dev_err = reinterpret_cast<uint32_t *>(static_cast<unsigned char *>(slot->scratch) + kMapBytes);
-    cudaError_t e = cudaMemsetAsync(ctx.dev_err, 0, 2 * sizeof(uint32_t), ctx.stream);
+    cudaError_t e = cudaMemsetAsync(ctx.dev_err, 0, 3 * sizeof(uint32_t), ctx.stream);
     if (e == cudaSuccess) {
         d.in_kind = t.in;
         d.out_kind = t.out;

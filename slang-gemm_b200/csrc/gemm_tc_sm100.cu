@@ -96,6 +96,8 @@ struct TcArgs {
     const CUtensorMap *b_maps;
     const uint32_t *skip_flag;   // pointer-array batches: == skip_gen when a pointer is not 16-byte aligned
     uint32_t skip_gen;
+    const CUtensorMap *c_maps;   // pointer-array batches with TMA-stored C: per-batch C maps in global memory
+    const uint32_t *c_skip_flag; // == skip_gen when a C pointer is not 16-byte aligned (C then stored directly)
     int tma_store;               // epilogue writes C with TMA tensor stores (beta == 0, C TMA-addressable)
     int ab_evict_last;           // operand loads use the evict_last L2 policy
     simt::SimtArgs fb;           // pointer-array batches: the CUDA-core fallback's view of the problem
@@ -334,6 +336,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int row = quad * 32 + lane;
         const uint32_t tempty_leader = CG == 2 ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
         const uint64_t pol_c = l2_policy_evict_first();
+        // TMA-stored C; pointer-array batches fall back to direct stores when a C entry is misaligned.
+        const bool c_tma = args.tma_store && !(args.c_skip_flag != nullptr && *args.c_skip_flag == args.skip_gen);
         int stg_flip = 0;
         int it = 0;
         bool ok = true;
@@ -345,6 +349,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (args.c_arr != nullptr) Cb = args.c_arr[b];
             else Cb = static_cast<uint8_t *>(args.C) + static_cast<size_t>(b) * args.stride_c *
                                                         ((OUT == OUT_F16 || OUT == OUT_BF16) ? 2 : 4);
+            const CUtensorMap *cmap = args.c_maps != nullptr ? args.c_maps + b : &tmC;
+            const int cz = args.c_maps != nullptr ? 0 : b;
+            if (c_tma && args.c_maps != nullptr && lane == 0) tensormap_acquire(cmap);
             // One pass per accumulator slot this tile owns: the tile's 256-column
             // buffer, or (WIDE) each half of the 512-column accumulator in turn.
 #pragma unroll 1
@@ -360,7 +367,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c, r);
                 tmem_wait_ld();
-                if (args.tma_store) {
+                if (c_tma) {
                     // Stage this warp's 32 rows in blocks of 16 columns (column-major, like C)
                     // and write each block with one TMA tensor store; edge elements are
                     // clipped by TMA. Two staging buffers per warp alternate.
@@ -393,8 +400,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         fence_proxy_async();
                         __syncwarp();
                         if (lane == 0) {
-                            tma_store_3d(&tmC, buf, mb * C_::TILE_M + static_cast<int>(rank) * BM + quad * 32,
-                                         n0 + c + 16 * h, b, pol_c);
+                            tma_store_3d(cmap, buf, mb * C_::TILE_M + static_cast<int>(rank) * BM + quad * 32,
+                                         n0 + c + 16 * h, cz, pol_c);
                             bulk_commit_group();
                         }
                     }
@@ -420,7 +427,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             }  // accumulator slots of this tile
         }
-        if (args.tma_store && lane == 0) bulk_wait_group_all();  // C is written before the kernel ends
+        if (c_tma && lane == 0) bulk_wait_group_all();  // C is written before the kernel ends
     }
 
     tc_fence_before();
@@ -440,14 +447,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // A pointer that is not 16-byte aligned cannot be a TMA base address: the
 // builder then writes this call's tag `gen` into *misaligned and the
 // tensor-core kernel computes the whole batch with its CUDA-core fallback
-// instead (a word tagged by an earlier call never matches).
-__global__ void k_build_ptr_maps(const CUtensorMap tmpl_a, const CUtensorMap tmpl_b, const void *const *a_arr,
-                                 const void *const *b_arr, CUtensorMap *maps_a, CUtensorMap *maps_b, int batch,
-                                 uint32_t *misaligned, uint32_t gen) {
+// instead (a word tagged by an earlier call never matches). C maps (written
+// when maps_c is not null) have their own flag: a misaligned C entry only
+// switches the epilogue to direct stores.
+__global__ void k_build_ptr_maps(const CUtensorMap tmpl_a, const CUtensorMap tmpl_b, const CUtensorMap tmpl_c,
+                                 const void *const *a_arr, const void *const *b_arr, void *const *c_arr,
+                                 CUtensorMap *maps_a, CUtensorMap *maps_b, CUtensorMap *maps_c, int batch,
+                                 uint32_t *misaligned, uint32_t *misaligned_c, uint32_t gen) {
     grid_dep_wait();
     grid_dep_launch();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= batch) return;
+    if (maps_c != nullptr) {
+        const uint64_t pc = reinterpret_cast<uint64_t>(c_arr[i]);
+        if ((pc & 15u) != 0u) {
+            atomicExch(misaligned_c, gen);
+        } else {
+            maps_c[i] = tmpl_c;
+            asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;"
+                         ::"l"(reinterpret_cast<uint64_t>(maps_c + i)), "l"(pc) : "memory");
+        }
+    }
     const uint64_t pa = reinterpret_cast<uint64_t>(a_arr[i]), pb = reinterpret_cast<uint64_t>(b_arr[i]);
     if (((pa | pb) & 15u) != 0u) {
         atomicExch(misaligned, gen);
@@ -683,7 +703,7 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     // Template maps over a placeholder (16-byte aligned, never dereferenced
     // through the template) with the per-batch geometry; the builder kernel
     // swaps in each batch entry's address.
-    const size_t need = 2 * static_cast<size_t>(d.batch) * sizeof(CUtensorMap);
+    const size_t need = 3 * static_cast<size_t>(d.batch) * sizeof(CUtensorMap);
     if (ctx.tmap_bytes < need) {
         if (ctx.tmap_buf) cudaFree(ctx.tmap_buf);
         ctx.tmap_buf = nullptr;
@@ -699,15 +719,24 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
         ctx.last_error = "tensor map encode failed: " + why;
         return cudaErrorInvalidValue;
     }
-    const CUtensorMap tcm = ta;  // pointer-array C is stored directly (no per-batch C map)
-    args.tma_store = 0;
+    // With beta == 0 C is written by TMA stores through per-entry maps (one
+    // batch entry each) built next to A's and B's; otherwise directly.
+    CUtensorMap tcm = ta;
+    GemmDesc dc = d;
+    dc.batch = 1;
+    dc.C = ctx.tmap_buf;
+    const bool c_tma = make_c_map(dc, &tcm);
+    args.tma_store = c_tma ? 1 : 0;
     CUtensorMap *maps_a = static_cast<CUtensorMap *>(ctx.tmap_buf);
     CUtensorMap *maps_b = maps_a + d.batch;
+    CUtensorMap *maps_c = c_tma ? maps_b + d.batch : nullptr;
     uint32_t *misaligned = ctx.dev_err + 1;
+    uint32_t *misaligned_c = ctx.dev_err + 2;
     const uint32_t gen = ctx.next_ptr_gen();
     const int threads = 128;
     cudaError_t e = launch_pdl(k_build_ptr_maps, dim3((d.batch + threads - 1) / threads), dim3(threads), 0, ctx.stream,
-                               1, ta, tb, a_arr, b_arr, maps_a, maps_b, d.batch, misaligned, gen);
+                               1, ta, tb, tcm, a_arr, b_arr, c_arr, maps_a, maps_b, maps_c, d.batch, misaligned,
+                               misaligned_c, gen);
     ctx.launches++;
     ctx.last_kernels |= GS_KERNEL_TMAP;
     if (e != cudaSuccess) return e;
@@ -718,6 +747,8 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     args.c_arr = c_arr;
     args.skip_flag = misaligned;
     args.skip_gen = gen;
+    args.c_maps = maps_c;
+    args.c_skip_flag = c_tma ? misaligned_c : nullptr;
     args.fb = simt::make_args(d, a_arr, b_arr, c_arr);
     return dispatch_shape(shape, ctx, d, ta, tb, tcm, args);
 }

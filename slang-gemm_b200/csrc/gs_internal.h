@@ -47,7 +47,7 @@ struct Context {
     int device = -1;
     int sm_count = 0;
     cudaStream_t stream = nullptr;
-    uint32_t *dev_err = nullptr;      // [0] error word of bounded waits, [1] pointer-array misalignment flag
+    uint32_t *dev_err = nullptr;      // [0] error word of bounded waits, [1] / [2] pointer-array A,B / C misalignment flags
     uint32_t last_kernels = 0;
     uint64_t launches = 0;
     std::string last_error;

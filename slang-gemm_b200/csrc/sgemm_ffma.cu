@@ -373,8 +373,8 @@ static long long ctas(const GemmDesc &d) {
 // Tile choice: the largest tile whose grid still gives every SM at least one
 // CTA; below that the 64 x 64 tile with K split over a cluster of S CTAs
 // (S the power of two, at most 8, that brings the grid to the SM count while
-// every CTA keeps at least two K steps); the 32 x 32 tile when K is too short
-// to split.
+// every CTA keeps at least two K steps, doubled once more for grids of at
+// most half the SM count); the 32 x 32 tile when K is too short to split.
 // a_arr/b_arr/c_arr: device arrays of per-entry pointers (pointer-array
 // batches), or nullptr for the strided layout of `d`.
 cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
@@ -397,12 +397,17 @@ cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *
     a.vec_c = d.ldc % 4 == 0 && (!strided || d.stride_c % 4 == 0);
     a.ep = d.ep;
     const long long sms = ctx.sm_count > 0 ? ctx.sm_count : 148;
-    if (ctas<TileL>(d) >= sms) return go_ops<TileL>(ctx, d, a);
     const long long cm = ctas<TileM>(d);
+    // op(A) = T with op(B) = N is the one 128 x 128 variant that spills at 128
+    // registers; the 64 x 64 tile is faster for it whenever its grid fills the GPU.
+    const bool tn = d.trans_a && !d.trans_b;
+    if (ctas<TileL>(d) >= sms && !(tn && cm >= sms)) return go_ops<TileL>(ctx, d, a);
     if (cm >= sms) return go_ops<TileM>(ctx, d, a);
     const int ksteps = (d.k + TileM::BK - 1) / TileM::BK;
     int split = 1;
     while (split < 8 && cm * split < sms && ksteps >= 4 * split) split *= 2;
+    // At most half the SMs' worth of tiles: one more doubling measured faster (512^3: 4 -> 8).
+    if (split > 1 && split < 8 && 2 * cm <= sms && ksteps >= 8 * split) split *= 2;
     if (split == 8) return go_ops<TileM, 8>(ctx, d, a);
     if (split == 4) return go_ops<TileM, 4>(ctx, d, a);
     if (split == 2) return go_ops<TileM, 2>(ctx, d, a);

@@ -290,6 +290,47 @@ def test_pointer_array_batched(handle, dt, misalign, algo):
     assert handle.device_error() == 0
 
 
+@pytest.mark.parametrize("dt,ct", [(gs.R_16F, gs.R_32F), (gs.R_16BF, gs.R_16BF), (gs.R_8I, gs.R_32I),
+                                   (gs.R_16F, gs.R_16F)])
+@pytest.mark.parametrize("c_shift_entry", [-1, 2])
+@pytest.mark.parametrize("algo", TILES)
+def test_pointer_array_tma_store_c(handle, dt, ct, c_shift_entry, algo):
+    """beta == 0 pointer-array batches write C with TMA stores through per-entry C maps built on the device; a C
+    entry that is not 16-byte aligned switches the whole call to direct stores. Ragged M/N, a padded ldc and bytes
+    between columns (and past each entry) that must stay untouched."""
+    import torch
+
+    rng = np.random.default_rng(50 + dt + ct + algo)
+    m, n, k, batch, pad = 300, 136, 96, 4, 8
+    ldc = m + pad
+    es_c = np.dtype(NP_OF[ct]).itemsize
+    a_list = [make_input(rng, m * k, dt) for _ in range(batch)]
+    b_list = [make_input(rng, k * n, dt) for _ in range(batch)]
+    c_list = [make_c(rng, ldc * n + 16, ct) for _ in range(batch)]
+    da = [to_dev(x) for x in a_list]
+    db = [to_dev(x) for x in b_list]
+    dc = [to_dev(x) for x in c_list]
+    shift = [1 if j == c_shift_entry else 0 for j in range(batch)]  # one element: 2 or 4 bytes
+    aptr = torch.tensor([t.data_ptr() for t in da], dtype=torch.int64, device="cuda")
+    bptr = torch.tensor([t.data_ptr() for t in db], dtype=torch.int64, device="cuda")
+    cptr = torch.tensor([t.data_ptr() + shift[j] * es_c for j, t in enumerate(dc)], dtype=torch.int64, device="cuda")
+    comp = gs.COMPUTE_32I if dt == gs.R_8I else gs.COMPUTE_32F
+    alpha = 3.0 if dt == gs.R_8I else 1.25
+    handle.gemm_batched_ex(0, 0, m, n, k, alpha, aptr, dt, m, bptr, dt, k, 0.0, cptr, ct, ldc, batch, comp,
+                           algo=algo)
+    refs = [x.copy() for x in c_list]
+    views = [r[shift[j]:] for j, r in enumerate(refs)]
+    assert orc.gemm_batched_ex(0, 0, m, n, k, alpha, a_list, dt, m, b_list, dt, k, 0.0, views, ct, ldc,
+                               compute_type=comp) == orc.OK
+    for j in range(batch):
+        got = to_host(dc[j])
+        mask = np.zeros(got.size, bool)
+        mask[shift[j] + (np.arange(n)[:, None] * ldc + np.arange(m)[None, :]).ravel()] = True
+        tol_dt = gs.R_32F if dt == gs.R_8I else (ct if ct in (gs.R_16F, gs.R_16BF) else dt)
+        assert_parity(got, refs[j], ct, tol_dt, mask=mask, c_before=c_list[j])
+    assert handle.device_error() == 0
+
+
 # ---- host-buffer mirror of gemm.gemmEx --------------------------------------
 
 @pytest.mark.parametrize("layout", [orc.COL_MAJOR, orc.ROW_MAJOR])
