@@ -25,8 +25,9 @@
 //    and, in the even CTA only, issues tcgen05.mma from one thread;
 //    tcgen05.commit frees shared-memory stages and publishes accumulators
 //    (to both CTAs of the pair for CG 2);
-//  - warps 2..9: epilogue, two warps per TMEM lane quadrant, each draining
-//    half of a 256-column accumulator (the wide tile's two halves in turn). tcgen05.ld gives each thread one
+//  - warps 2..9 (2..17 for the wide tile): epilogue, two (four) warps per
+//    TMEM lane quadrant, each draining half (a quarter) of a 256-column
+//    accumulator (the wide tile's two halves in turn). tcgen05.ld gives each thread one
 //    accumulator row; with beta == 0 a warp stages 32 rows x 16 columns in
 //    shared memory (column-major, like C) and writes them with a TMA tensor
 //    store (L2 evict_first); otherwise the 32 lanes store 32 consecutive rows
@@ -49,9 +50,6 @@ constexpr int BM = 128;        // accumulator rows per CTA
 constexpr int BN = 256;        // accumulator columns per tcgen05.mma (and per tile unless wide)
 constexpr int BK_BYTES = 128;  // K bytes per stage
 constexpr int TMEM_COLS = 2 * BN;
-// Epilogue warps: two per TMEM lane quadrant, each draining half of the columns.
-constexpr int EPI_WARPS = 8;
-constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 // Result stores are streamed through L2 (evict_first) so the output does not
 // push operand panels out; operand loads of a single GEMM are kept
 // (evict_last: its A and B panels are re-read by many tiles), those of batched
@@ -68,6 +66,12 @@ template <int CG, bool WIDE>
 struct Cfg {
     static constexpr int TILE_N = WIDE ? 2 * BN : BN;      // columns of one tile
     static constexpr int NSUB = TILE_N / BN;               // tcgen05.mma per K step
+    // Epilogue warps: EPI_WARPS / 4 per TMEM lane quadrant, each draining EPI_COLS
+    // columns of an accumulator slot. The wide tile's MMAs wait for its drain,
+    // so it gets twice the warps (it has the registers: no CUDA-core fallback).
+    static constexpr int EPI_WARPS = WIDE ? 16 : 8;
+    static constexpr int EPI_COLS = BN / (EPI_WARPS / 4);
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr int STAGES = WIDE ? 4 : (CG == 2 ? 6 : 4);
     static constexpr int B_BOX = BN / CG;                  // B columns per TMA box (one per sub-MMA)
     static constexpr int B_ROWS = NSUB * B_BOX;            // B columns this CTA loads per tile
@@ -76,9 +80,11 @@ struct Cfg {
     static constexpr int B_STAGE = B_ROWS * BK_BYTES;      // 16 KiB (CG 2) / 32 KiB (CG 1, CG 2 wide)
     static constexpr int STAGE = A_STAGE + B_STAGE;
     static constexpr int TILE_M = BM * CG;                 // rows of one (pair) tile
-    // Epilogue staging for TMA stores: per epilogue warp two 32-row x 16-column x 4-byte blocks.
+    // Epilogue staging for TMA stores: per epilogue warp NSTG 32-row x 16-column x 4-byte blocks
+    // (the wide tile's 16 warps get one each, which keeps its four operand stages).
     static constexpr int STG_BLOCK = 32 * 16 * 4;
-    static constexpr int STG_BYTES = EPI_WARPS * 2 * STG_BLOCK;  // 32 KiB
+    static constexpr int NSTG = WIDE ? 1 : 2;
+    static constexpr int STG_BYTES = EPI_WARPS * NSTG * STG_BLOCK;
     static constexpr int SMEM = STAGES * STAGE + STG_BYTES + 1024 /*alignment slack*/ + 256 /*barriers*/;
 };
 
@@ -118,7 +124,7 @@ __device__ __forceinline__ void tile_coords(const TcArgs &a, long long t, int &b
 }
 
 template <int IN, int OUT, int CG, bool WIDE>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmC, const TcArgs args) {
     using C_ = Cfg<CG, WIDE>;
@@ -155,9 +161,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // the same word and, instead of the tensor-core pipeline, runs the CUDA-core
     // tile loop over the whole batch (both CTAs of a pair take the same path,
     // before any cluster barrier or TMEM allocation).
-    if (args.skip_flag != nullptr && *args.skip_flag == args.skip_gen) {
-        simt::simt_tiles<IN, OUT>(args.fb, blockIdx.x, gridDim.x, smem);
-        return;
+    if constexpr (!WIDE) {  // pointer-array batches never use the wide tile
+        if (args.skip_flag != nullptr && *args.skip_flag == args.skip_gen) {
+            simt::simt_tiles<IN, OUT>(args.fb, blockIdx.x, gridDim.x, smem);
+            return;
+        }
     }
 
     if (threadIdx.x == 0) {
@@ -168,7 +176,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
             // One elected lane per epilogue warp (of both CTAs for CG 2).
-            mbar_init(&tempty[i], CG * EPI_WARPS);
+            mbar_init(&tempty[i], CG * C_::EPI_WARPS);
         }
         fence_barrier_init();
     }
@@ -330,9 +338,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else {
         // ---------------- epilogue warps 2..2+EPI_WARPS-1 (both CTAs) ----------------
-        const int quad = warp & 3;               // TMEM lane quadrant this warp may access
-        const int ew = warp - 2;                 // epilogue warp index
-        const int c_lo = (ew / 4) * (BN / 2);    // this warp's half of the accumulator columns
+        const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
+        const int ew = warp - 2;                    // epilogue warp index
+        const int c_lo = (ew / 4) * C_::EPI_COLS;   // this warp's share of the accumulator columns
         const int row = quad * 32 + lane;
         const uint32_t tempty_leader = CG == 2 ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
         const uint64_t pol_c = l2_policy_evict_first();
@@ -363,7 +371,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int n0 = nb * TILE_N + half * BN;  // tile column of this slot's first accumulator column
             const int ncols = min(BN, args.n - n0);
 #pragma unroll 1
-            for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
+            for (int c = c_lo; c < c_lo + C_::EPI_COLS; c += 32) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c, r);
                 tmem_wait_ld();
@@ -374,9 +382,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         if (c + 16 * h >= ncols) continue;
-                        uint8_t *buf = stg + (ew * 2 + stg_flip) * C_::STG_BLOCK;
-                        stg_flip ^= 1;
-                        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` has read it
+                        uint8_t *buf = stg + (ew * C_::NSTG + stg_flip) * C_::STG_BLOCK;
+                        stg_flip = stg_flip + 1 == C_::NSTG ? 0 : stg_flip + 1;
+                        if (lane == 0) bulk_wait_group_read<C_::NSTG - 1>();  // the store that last used `buf` has read it
                         __syncwarp();
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
@@ -482,15 +490,17 @@ __global__ void k_build_ptr_maps(const CUtensorMap tmpl_a, const CUtensorMap tmp
     asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
 }
 
-// Largest number of co-resident CTA pairs for the 2-SM kernel on this device.
-template <typename K>
-static int max_pairs(Context &ctx, K kern, int smem) {
-    static int cached[64] = {};
+// Largest number of co-resident CTA pairs for one 2-SM kernel instantiation on this device.
+template <int IN, int OUT, int CG, bool WIDE>
+static int max_pairs(Context &ctx) {
+    using C_ = Cfg<CG, WIDE>;
+    auto kern = k_gemm_tc<IN, OUT, CG, WIDE>;
+    static int cached[64] = {};  // per instantiation and device
     if (ctx.device >= 0 && ctx.device < 64 && cached[ctx.device] > 0) return cached[ctx.device];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (ctx.sm_count / 2), 1, 1);
-    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem;
+    cfg.blockDim = dim3(C_::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C_::SMEM;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = 2;
@@ -520,15 +530,15 @@ static cudaError_t launch_kernel(Context &ctx, const CUtensorMap &ta, const CUte
         if (ctx.device >= 0 && ctx.device < 64) attr_set[ctx.device] = true;
     }
     if constexpr (CG == 2) {
-        const long long pairs = args.total_tiles < max_pairs(ctx, kern, C_::SMEM) ? args.total_tiles
-                                                                                 : max_pairs(ctx, kern, C_::SMEM);
-        e = launch_pdl(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(NUM_THREADS), C_::SMEM, ctx.stream, 2, ta,
+        const long long mp = max_pairs<IN, OUT, CG, WIDE>(ctx);
+        const long long pairs = args.total_tiles < mp ? args.total_tiles : mp;
+        e = launch_pdl(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(C_::THREADS), C_::SMEM, ctx.stream, 2, ta,
                        tb, tcm, args);
         ctx.launches++;
         return e;
     } else {
         const long long grid = args.total_tiles < ctx.sm_count ? args.total_tiles : ctx.sm_count;
-        e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(NUM_THREADS), C_::SMEM, ctx.stream, 1, ta, tb,
+        e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(C_::THREADS), C_::SMEM, ctx.stream, 1, ta, tb,
                        tcm, args);
         ctx.launches++;
         return e;
@@ -697,7 +707,8 @@ cudaError_t launch_tc(Context &ctx, const GemmDesc &d) {
 cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
                                 void *const *c_arr) {
     using namespace tc;
-    const int shape = choose_shape(ctx, d);
+    // The wide tile has no CUDA-core fallback for misaligned entries: pair tile instead.
+    const int shape = choose_shape(ctx, d) == 3 ? 2 : choose_shape(ctx, d);
     const int cg = shape == 1 ? 1 : 2;
     TcArgs args = make_args(ctx, d, shape);
     // Template maps over a placeholder (16-byte aligned, never dereferenced
