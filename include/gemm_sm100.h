@@ -101,7 +101,8 @@ enum {
     GS_KERNEL_FFMA = 1u << 3,     /* register-blocked FFMA sgemm */
     GS_KERNEL_SIMT = 1u << 4,     /* generic CUDA-core kernel for operands TMA cannot address */
     GS_KERNEL_SCALE = 1u << 5,    /* C = beta*C for k == 0 */
-    GS_KERNEL_TMAP = 1u << 6      /* device-side tensor-map builder (pointer-array batches) */
+    GS_KERNEL_TMAP = 1u << 6,     /* device-side tensor-map builder (pointer-array batches) */
+    GS_KERNEL_TC_TF32 = 1u << 7   /* COMPUTE_32F_FAST_TF32: operand split + tcgen05 kind::tf32 */
 };
 
 /* ---------------------------------------------------------------------- */
@@ -134,6 +135,10 @@ gs_status gs_hgemm(gs_handle handle, int transa, int transb, int m, int n, int k
  *   A,B = R_16F,  C = R_16F,           compute 16F (alpha/beta f16 bits)           (tcgen05)
  *   A,B = R_8I,   C = R_32I,           compute 32I / 32I_PEDANTIC                  (tcgen05)
  *   A,B,C = R_32F,                     compute 32F / 32F_PEDANTIC                  (FFMA)
+ *   A,B,C = R_32F,                     compute 32F_FAST_TF32: problems of at least a GFLOP with
+ *                                      k <= 384 on the tensor cores, each f32 product as three
+ *                                      tf32 products (hi*hi + hi*lo + lo*hi), within the FP32
+ *                                      tolerance; everything else on FFMA
  * Anything else returns GS_STATUS_NOT_SUPPORTED. INT8 requires k <= 131071 so
  * that the s32 accumulator cannot overflow. */
 gs_status gs_gemm_ex(gs_handle handle, int transa, int transb, int m, int n, int k,

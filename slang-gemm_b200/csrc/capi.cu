@@ -16,7 +16,7 @@
 
 namespace gs {
 
-size_t in_elem_size(InKind k) { return k == IN_I8 ? 1 : (k == IN_F32 ? 4 : 2); }
+size_t in_elem_size(InKind k) { return k == IN_I8 ? 1 : ((k == IN_F32 || k == IN_TF32) ? 4 : 2); }
 size_t out_elem_size(OutKind k) { return (k == OUT_F16 || k == OUT_BF16) ? 2 : 4; }
 
 // ---- tensor-map encoder (driver entry point, resolved once) --------------
@@ -71,7 +71,7 @@ gs_status plan_gemm(const GemmDesc &d, Plan *plan, std::string *why) {
         return GS_STATUS_SUCCESS;
     }
     if (d.in_kind == IN_F32) {
-        plan->kernel = GS_KERNEL_FFMA;
+        plan->kernel = d.fast_tf32 && tf32_worthwhile(d) ? GS_KERNEL_TC_TF32 : GS_KERNEL_FFMA;
         return GS_STATUS_SUCCESS;
     }
     const long long es = static_cast<long long>(in_elem_size(d.in_kind));
@@ -159,6 +159,7 @@ gs_status gs_destroy(gs_handle h) {
     if (h->ctx.dev_err) cudaFree(h->ctx.dev_err);
     if (h->ctx.stage) cudaFree(h->ctx.stage);
     if (h->ctx.tmap_buf) cudaFree(h->ctx.tmap_buf);
+    if (h->ctx.tf32_buf) cudaFree(h->ctx.tf32_buf);
     if (h->ctx.h2d) cudaStreamDestroy(h->ctx.h2d);
     if (h->ctx.d2h) cudaStreamDestroy(h->ctx.d2h);
     if (h->ctx.ev_start) cudaEventDestroy(h->ctx.ev_start);
@@ -232,7 +233,8 @@ gs_status decode_types(int at, int bt, int ct, int comp, TypedArgs *t) {
         return GS_STATUS_NOT_SUPPORTED;
     }
     if (at == GS_R_32F) {
-        // FAST_TF32 permits, and does not require, TF32 products: it runs the exact-f32 FFMA kernel.
+        // FAST_TF32 permits TF32 products: large short-K problems run on the tensor cores
+        // with three tf32 products per f32 product (within the f32 tolerance), the rest on FFMA.
         if ((c32f || comp == GS_COMPUTE_32F_FAST_TF32) && ct == GS_R_32F) { *t = {IN_F32, OUT_F32}; return GS_STATUS_SUCCESS; }
         return GS_STATUS_NOT_SUPPORTED;
     }
@@ -322,6 +324,15 @@ gs_status run(gs_handle h, GemmDesc &d) {
     case 0: return GS_STATUS_SUCCESS;
     case GS_KERNEL_SCALE: e = launch_scale(ctx, d, nullptr); break;
     case GS_KERNEL_FFMA: e = launch_ffma(ctx, d); break;
+    case GS_KERNEL_TC_TF32:
+        e = launch_tf32(ctx, d);
+        if (e == cudaErrorMemoryAllocation || e == cudaErrorInvalidValue) {
+            // No room for the split operands, or a geometry TMA refuses: the exact FFMA kernel.
+            cudaGetLastError();
+            plan.kernel = GS_KERNEL_FFMA;
+            e = launch_ffma(ctx, d);
+        }
+        break;
     case GS_KERNEL_SIMT: e = launch_simt(ctx, d, nullptr, nullptr, nullptr); break;
     default:
         e = launch_tc(ctx, d);
@@ -378,6 +389,7 @@ gs_status gs_gemm_strided_batched_ex(gs_handle h, int transa, int transb, int m,
     d.stride_a = strideA;
     d.stride_b = strideB;
     d.stride_c = strideC;
+    d.fast_tf32 = t.in == IN_F32 && computeType == GS_COMPUTE_32F_FAST_TF32;
     read_scalars(computeType, alpha, beta, &d.ep);
     return run(h, d);
 }
@@ -403,6 +415,7 @@ gs_status gs_plan_gemm_strided_batched_ex(int transa, int transb, int m, int n, 
     d.A = A;
     d.B = B;
     d.C = const_cast<void *>(C);
+    d.fast_tf32 = t.in == IN_F32 && computeType == GS_COMPUTE_32F_FAST_TF32;
     d.stride_a = strideA;
     d.stride_b = strideB;
     d.stride_c = strideC;

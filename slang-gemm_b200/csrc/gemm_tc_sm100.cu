@@ -131,13 +131,13 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
     static_assert(!WIDE || CG == 2, "the wide tile is a CTA-pair tile");
     constexpr int STAGES = C_::STAGES;
     constexpr int TILE_N = C_::TILE_N;
-    constexpr int ES = (IN == IN_I8) ? 1 : 2;          // element bytes
+    constexpr int ES = (IN == IN_I8) ? 1 : (IN == IN_TF32 ? 4 : 2);  // element bytes
     constexpr int BK = BK_BYTES / ES;                  // K elements per stage
-    constexpr int UK = (IN == IN_I8) ? 32 : 16;        // K per tcgen05.mma
+    constexpr int UK = 32 / ES;                        // K per tcgen05.mma (32 bytes)
     constexpr int CH = BK_BYTES / ES;                  // MN elements per 128-byte swizzle panel
     constexpr uint32_t CH_BYTES = CH * BK * ES;        // bytes of one MN-major panel (BK rows x 128 B)
     constexpr uint32_t C_FMT = (IN == IN_I8) ? 2u : 1u;
-    constexpr uint32_t AB_FMT = (IN == IN_F16) ? 0u : 1u;  // bf16 = 1, s8 = 1
+    constexpr uint32_t AB_FMT = (IN == IN_F16) ? 0u : (IN == IN_TF32 ? 2u : 1u);  // bf16 = 1, s8 = 1, tf32 = 2
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
     // the same word and, instead of the tensor-core pipeline, runs the CUDA-core
     // tile loop over the whole batch (both CTAs of a pair take the same path,
     // before any cluster barrier or TMEM allocation).
-    if constexpr (!WIDE) {  // pointer-array batches never use the wide tile
+    if constexpr (!WIDE && IN != IN_TF32) {  // pointer-array batches never use the wide tile or tf32
         if (args.skip_flag != nullptr && *args.skip_flag == args.skip_gen) {
             simt::simt_tiles<IN, OUT>(args.fb, blockIdx.x, gridDim.x, smem);
             return;
@@ -319,9 +319,11 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                             const uint32_t d = d_tmem + s * BN;
                             if constexpr (CG == 2) {
                                 if constexpr (IN == IN_I8) umma_i8_2sm(d, adesc, bdesc, idesc, accum);
+                                else if constexpr (IN == IN_TF32) umma_tf32_2sm(d, adesc, bdesc, idesc, accum);
                                 else umma_f16_2sm(d, adesc, bdesc, idesc, accum);
                             } else {
                                 if constexpr (IN == IN_I8) umma_i8(d, adesc, bdesc, idesc, accum);
+                                else if constexpr (IN == IN_TF32) umma_tf32(d, adesc, bdesc, idesc, accum);
                                 else umma_f16(d, adesc, bdesc, idesc, accum);
                             }
                         }
@@ -560,6 +562,9 @@ static cudaError_t dispatch(Context &ctx, const GemmDesc &d, const CUtensorMap &
     case IN_I8:
         if (d.out_kind == OUT_I32) return launch_kernel<IN_I8, OUT_I32, CG, WIDE>(ctx, ta, tb, tcm, args);
         break;
+    case IN_TF32:
+        if (d.out_kind == OUT_F32) return launch_kernel<IN_TF32, OUT_F32, CG, WIDE>(ctx, ta, tb, tcm, args);
+        break;
     default: break;
     }
     return cudaErrorInvalidValue;
@@ -574,8 +579,10 @@ static cudaError_t dispatch_shape(int shape, Context &ctx, const GemmDesc &d, co
 }
 
 static CUtensorMapDataType tmap_dtype(InKind k) {
-    return k == IN_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                       : (k == IN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8);
+    return k == IN_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+           : k == IN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+           : k == IN_TF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                          : CU_TENSOR_MAP_DATA_TYPE_UINT8;
 }
 
 // Encodes the A and B maps. `batch_a`/`batch_b` are the extents of the third

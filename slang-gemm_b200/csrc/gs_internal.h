@@ -11,7 +11,9 @@
 namespace gs {
 
 // Element / output kinds the kernels are specialised on.
-enum InKind { IN_F16 = 0, IN_BF16 = 1, IN_I8 = 2, IN_F32 = 3 };
+// IN_TF32: fp32 storage read by tcgen05 kind::tf32 (the operands the FAST_TF32
+// path prepares, each value split into two tf32-exact parts).
+enum InKind { IN_F16 = 0, IN_BF16 = 1, IN_I8 = 2, IN_F32 = 3, IN_TF32 = 4 };
 enum OutKind { OUT_F32 = 0, OUT_I32 = 1, OUT_F16 = 2, OUT_BF16 = 3 };
 
 // Epilogue scalars. Which fields are used depends on the output / compute kind.
@@ -35,6 +37,7 @@ struct GemmDesc {
     void *C; long long ldc, stride_c;
     Epilogue ep;
     int algo;                 // cublasGemmAlgo_t hint: 0 = 1-SM tile, 1 = 2-SM pair tile, else automatic
+    int fast_tf32;            // COMPUTE_32F_FAST_TF32 on f32 operands: TF32 tensor-core products allowed
 };
 
 // Kernel selection made by plan_gemm (pure host logic, no device calls).
@@ -62,6 +65,9 @@ struct Context {
     // device copy of tensor maps for pointer-array batches
     void *tmap_buf = nullptr;
     size_t tmap_bytes = 0;
+    // split operands of the FAST_TF32 tensor-core path
+    void *tf32_buf = nullptr;
+    size_t tf32_bytes = 0;
     // Pointer-array calls tag the misalignment word with a per-call value
     // instead of clearing it first (one stream operation less per call).
     uint32_t ptr_gen = 0;
@@ -110,6 +116,11 @@ gs_status plan_gemm(const GemmDesc &d, Plan *plan, std::string *why);
 
 // Launchers (return cudaSuccess or the launch error).
 cudaError_t launch_tc(Context &ctx, const GemmDesc &d);
+// FAST_TF32 f32 GEMM on the tensor cores: splits A and B into tf32-exact
+// high/low parts and runs one kind::tf32 GEMM over the concatenated K.
+cudaError_t launch_tf32(Context &ctx, const GemmDesc &d);
+// Whether a FAST_TF32 problem is large enough for the tensor-core path to win.
+bool tf32_worthwhile(const GemmDesc &d);
 cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *const *a_arr,
                                 const void *const *b_arr, void *const *c_arr);
 cudaError_t launch_ffma(Context &ctx, const GemmDesc &d);

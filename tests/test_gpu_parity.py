@@ -407,6 +407,23 @@ def test_fp32_fast_tf32_runs_exact_ffma(handle, op_a, op_b):
              comp=gs.COMPUTE_32F_FAST_TF32)
 
 
+@pytest.mark.parametrize("op_a,op_b,m,n,k,batch,pad,bcast_a,kernel", [
+    (0, 0, 2048, 1024, 256, 1, (0, 0, 0), False, gs.KERNEL_TC_TF32),
+    (1, 0, 1536, 1024, 383, 1, (3, 1, 2), False, gs.KERNEL_TC_TF32),   # K not a multiple of 4, unaligned lds
+    (0, 1, 1024, 2048, 300, 1, (0, 0, 0), False, gs.KERNEL_TC_TF32),
+    (1, 1, 1024, 1024, 200, 3, (0, 0, 0), False, gs.KERNEL_TC_TF32),   # strided batch
+    (0, 0, 1024, 2048, 256, 2, (0, 0, 0), True, gs.KERNEL_TC_TF32),    # broadcast A (stride 0)
+    (2, 2, 1100, 1300, 350, 1, (1, 0, 5), False, gs.KERNEL_TC_TF32),   # op C, ragged tiles
+    (0, 0, 1024, 512, 2048, 1, (0, 0, 0), False, gs.KERNEL_FFMA),      # K past the tf32 bound: exact FFMA
+])
+def test_fast_tf32_tensor_cores(handle, op_a, op_b, m, n, k, batch, pad, bcast_a, kernel):
+    """COMPUTE_32F_FAST_TF32 on large short-K problems runs tcgen05 kind::tf32 over the split operands (three tf32
+    products per f32 product) and must still meet the FP32 normwise tolerance against the oracle; longer K stays on
+    the exact FFMA kernel."""
+    run_case(handle, gs.R_32F, op_a, op_b, m, n, k, alpha=1.5, beta=-0.5, pad=pad, batch=batch, bcast_a=bcast_a,
+             seed=m + n + k + batch, comp=gs.COMPUTE_32F_FAST_TF32, expect_kernel=kernel)
+
+
 @pytest.mark.parametrize("m,n,k", [(32, 32, 40), (96, 64, 33), (200, 136, 260), (1000, 1000, 64),
                                    (2040, 1288, 72)])
 @pytest.mark.parametrize("op_a,op_b", [(0, 0), (1, 0), (0, 1), (1, 1)])
