@@ -135,10 +135,10 @@ gs_status gs_hgemm(gs_handle handle, int transa, int transb, int m, int n, int k
  *   A,B = R_16F,  C = R_16F,           compute 16F (alpha/beta f16 bits)           (tcgen05)
  *   A,B = R_8I,   C = R_32I,           compute 32I / 32I_PEDANTIC                  (tcgen05)
  *   A,B,C = R_32F,                     compute 32F / 32F_PEDANTIC                  (FFMA)
- *   A,B,C = R_32F,                     compute 32F_FAST_TF32: problems of at least a GFLOP with
- *                                      k <= 384 on the tensor cores, each f32 product as three
- *                                      tf32 products (hi*hi + hi*lo + lo*hi), within the FP32
- *                                      tolerance; everything else on FFMA
+ *   A,B,C = R_32F,                     compute 32F_FAST_TF32: problems of at least a GFLOP on the
+ *                                      tensor cores, each f32 product as three tf32 products
+ *                                      (hi*hi + hi*lo + lo*hi), K accumulated in chunks added in
+ *                                      f32, within the FP32 tolerance; smaller ones on FFMA
  * Anything else returns GS_STATUS_NOT_SUPPORTED. INT8 requires k <= 131071 so
  * that the s32 accumulator cannot overflow. */
 gs_status gs_gemm_ex(gs_handle handle, int transa, int transb, int m, int n, int k,

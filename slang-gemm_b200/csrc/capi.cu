@@ -233,8 +233,8 @@ gs_status decode_types(int at, int bt, int ct, int comp, TypedArgs *t) {
         return GS_STATUS_NOT_SUPPORTED;
     }
     if (at == GS_R_32F) {
-        // FAST_TF32 permits TF32 products: large short-K problems run on the tensor cores
-        // with three tf32 products per f32 product (within the f32 tolerance), the rest on FFMA.
+        // FAST_TF32 permits TF32 products: large problems run on the tensor cores with three
+        // tf32 products per f32 product (within the f32 tolerance), small ones on FFMA.
         if ((c32f || comp == GS_COMPUTE_32F_FAST_TF32) && ct == GS_R_32F) { *t = {IN_F32, OUT_F32}; return GS_STATUS_SUCCESS; }
         return GS_STATUS_NOT_SUPPORTED;
     }

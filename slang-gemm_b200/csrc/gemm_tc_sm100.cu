@@ -49,6 +49,7 @@ namespace tc {
 constexpr int BM = 128;        // accumulator rows per CTA
 constexpr int BN = 256;        // accumulator columns per tcgen05.mma (and per tile unless wide)
 constexpr int BK_BYTES = 128;  // K bytes per stage
+constexpr int CHUNK_KB = 36;   // TF32: stages per accumulator fill (1152 K elements, 144 tcgen05.mma)
 constexpr int TMEM_COLS = 2 * BN;
 // Result stores are streamed through L2 (evict_first) so the output does not
 // push operand panels out; operand loads of a single GEMM are kept
@@ -138,6 +139,13 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
     constexpr uint32_t CH_BYTES = CH * BK * ES;        // bytes of one MN-major panel (BK rows x 128 B)
     constexpr uint32_t C_FMT = (IN == IN_I8) ? 2u : 1u;
     constexpr uint32_t AB_FMT = (IN == IN_F16) ? 0u : (IN == IN_TF32 ? 2u : 1u);  // bf16 = 1, s8 = 1, tf32 = 2
+    // TF32 (the split FAST_TF32 operands): the tensor core's f32 accumulation
+    // loses a fraction of an ulp toward zero per accumulate step, so K is
+    // accumulated in chunks of CHUNK_KB stages in TMEM columns [0, 256) and the
+    // epilogue adds each chunk into a running sum in columns [256, 512) with
+    // exact f32 adds; only the last chunk's sum is stored.
+    constexpr bool CHUNKED = IN == IN_TF32;
+    static_assert(!CHUNKED || !WIDE, "the chunked accumulation needs the second TMEM half");
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -289,13 +297,22 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                 if constexpr (CG == 2) umma_commit_2sm(bar, 0x3);
                 else umma_commit(bar);
             };
+            uint32_t chunks = 0;  // CHUNKED: accumulator fills issued so far
             for (long long t = tile0; ok && t < args.total_tiles; t += tile_step, ++it) {
-                const int acc = WIDE ? 0 : (it & 1);
+                const int acc = (WIDE || CHUNKED) ? 0 : (it & 1);
                 const uint32_t acc_phase = WIDE ? (it & 1) : ((it >> 1) & 1);
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, 2)) break;
-                tc_fence_after();
+                if constexpr (!CHUNKED) {
+                    if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, 2)) break;
+                    tc_fence_after();
+                }
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 for (int kb = 0; kb < args.k_blocks; ++kb) {
+                    const int kb_in = CHUNKED ? kb % CHUNK_KB : kb;  // stage within the accumulator fill
+                    if (CHUNKED && kb_in == 0) {
+                        // the epilogue has folded the previous fill into the running sum
+                        if (!mbar_wait(&tempty[0], (chunks & 1u) ^ 1u, args.err, 2)) { ok = false; break; }
+                        tc_fence_after();
+                    }
                     if (!mbar_wait(&full[stage], phase, args.err, 3)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_base = smem_u32(smA + stage * C_::A_STAGE);
@@ -315,7 +332,7 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                             const uint64_t bdesc = args.b_mn
                                                        ? umma_smem_desc_sw128(b_base + kk * UK * 128, CH_BYTES, 1024)
                                                        : umma_smem_desc_sw128(b_base + kk * UK * ES, 16, 1024);
-                            const uint32_t accum = (kb | kk) != 0;
+                            const uint32_t accum = (kb_in | kk) != 0;
                             const uint32_t d = d_tmem + s * BN;
                             if constexpr (CG == 2) {
                                 if constexpr (IN == IN_I8) umma_i8_2sm(d, adesc, bdesc, idesc, accum);
@@ -334,8 +351,12 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     if (!ok) break;
                     commit_to(&empty[stage]);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    if (CHUNKED && (kb_in == CHUNK_KB - 1 || kb + 1 == args.k_blocks)) {
+                        commit_to(&tfull[0]);
+                        ++chunks;
+                    }
                 }
-                if (ok) commit_to(&tfull[WIDE ? 1 : acc]);
+                if (ok && !CHUNKED) commit_to(&tfull[WIDE ? 1 : acc]);
             }
         }
     } else {
@@ -350,11 +371,47 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
         const bool c_tma = args.tma_store && !(args.c_skip_flag != nullptr && *args.c_skip_flag == args.skip_gen);
         int stg_flip = 0;
         int it = 0;
+        uint32_t echunks = 0;  // CHUNKED: accumulator fills consumed so far
+        const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+        auto arrive_tempty = [&](int acc) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (CG == 2) mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
+                else mbar_arrive(&tempty[acc]);
+            }
+        };
         bool ok = true;
         for (long long t = tile0; ok && t < args.total_tiles; t += tile_step, ++it) {
             int b, mb, nb;
             tile_coords(args, t, b, mb, nb);
             const int m = mb * C_::TILE_M + static_cast<int>(rank) * BM + row;
+            const int nfills = CHUNKED ? (args.k_blocks + CHUNK_KB - 1) / CHUNK_KB : 1;
+            if constexpr (CHUNKED) {
+                // Fold every fill but the last into the running sum (columns BN..2BN-1), in order.
+#pragma unroll 1
+                for (int f = 0; ok && f + 1 < nfills; ++f) {
+                    if (!mbar_wait(&tfull[0], echunks & 1u, args.err, 4)) { ok = false; break; }
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c = c_lo; c < c_lo + C_::EPI_COLS; c += 32) {
+                        uint32_t r[32], sum[32];
+                        tmem_ld_32x32b_x32(t_lane + c, r);
+                        if (f > 0) tmem_ld_32x32b_x32(t_lane + BN + c, sum);
+                        tmem_wait_ld();
+                        if (f > 0) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                r[j] = __float_as_uint(__fadd_rn(__uint_as_float(sum[j]), __uint_as_float(r[j])));
+                        }
+                        tmem_st_32x32b_x32(t_lane + BN + c, r);
+                    }
+                    tmem_wait_st();
+                    arrive_tempty(0);
+                    ++echunks;
+                }
+                if (!ok) break;
+            }
             void *Cb = args.C;
             if (args.c_arr != nullptr) Cb = args.c_arr[b];
             else Cb = static_cast<uint8_t *>(args.C) + static_cast<size_t>(b) * args.stride_c *
@@ -366,8 +423,8 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
             // buffer, or (WIDE) each half of the 512-column accumulator in turn.
 #pragma unroll 1
             for (int half = 0; half < C_::NSUB; ++half) {
-            const int acc = WIDE ? half : (it & 1);
-            const uint32_t acc_phase = WIDE ? (it & 1) : ((it >> 1) & 1);
+            const int acc = WIDE ? half : (CHUNKED ? 0 : (it & 1));
+            const uint32_t acc_phase = CHUNKED ? (echunks & 1u) : (WIDE ? (it & 1) : ((it >> 1) & 1));
             if (!mbar_wait(&tfull[acc], acc_phase, args.err, 4)) { ok = false; break; }
             tc_fence_after();
             const int n0 = nb * TILE_N + half * BN;  // tile column of this slot's first accumulator column
@@ -375,8 +432,17 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
 #pragma unroll 1
             for (int c = c_lo; c < c_lo + C_::EPI_COLS; c += 32) {
                 uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + c, r);
-                tmem_wait_ld();
+                tmem_ld_32x32b_x32(t_lane + acc * BN + c, r);
+                if (CHUNKED && nfills > 1) {
+                    uint32_t sum[32];
+                    tmem_ld_32x32b_x32(t_lane + BN + c, sum);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        r[j] = __float_as_uint(__fadd_rn(__uint_as_float(sum[j]), __uint_as_float(r[j])));
+                } else {
+                    tmem_wait_ld();
+                }
                 if (c_tma) {
                     // Stage this warp's 32 rows in blocks of 16 columns (column-major, like C)
                     // and write each block with one TMA tensor store; edge elements are
@@ -429,12 +495,8 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     }
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if constexpr (CG == 2) mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
-                else mbar_arrive(&tempty[acc]);
-            }
+            arrive_tempty(acc);
+            if (CHUNKED) ++echunks;
             }  // accumulator slots of this tile
         }
         if (c_tma && lane == 0) bulk_wait_group_all();  // C is written before the kernel ends
@@ -562,8 +624,10 @@ static cudaError_t dispatch(Context &ctx, const GemmDesc &d, const CUtensorMap &
     case IN_I8:
         if (d.out_kind == OUT_I32) return launch_kernel<IN_I8, OUT_I32, CG, WIDE>(ctx, ta, tb, tcm, args);
         break;
-    case IN_TF32:
-        if (d.out_kind == OUT_F32) return launch_kernel<IN_TF32, OUT_F32, CG, WIDE>(ctx, ta, tb, tcm, args);
+    case IN_TF32:  // chunked accumulation: never the wide tile
+        if constexpr (!WIDE) {
+            if (d.out_kind == OUT_F32) return launch_kernel<IN_TF32, OUT_F32, CG, WIDE>(ctx, ta, tb, tcm, args);
+        }
         break;
     default: break;
     }
@@ -676,7 +740,13 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int shape) {
 // tile wins at 8192^3 and 4096^3 and for batch-256 512x512x1024 FP16; the
 // 256 x 256 tile wins for batch-64 2048^3 INT8, whose epilogue is busy 2/3 of
 // the time.)
+static int choose_shape_any(const GemmDesc &d);
 static int choose_shape(const Context &, const GemmDesc &d) {
+    const int shape = choose_shape_any(d);
+    // TF32 keeps a running sum in the second TMEM half, which the wide tile uses.
+    return shape == 3 && d.in_kind == IN_TF32 ? 2 : shape;
+}
+static int choose_shape_any(const GemmDesc &d) {
     if (d.algo == 0) return 1;
     if (d.algo == 1) return 2;
     if (d.algo == 2) return 3;

@@ -16,13 +16,15 @@
 // the usual alpha/beta epilogue. Non-finite inputs are outside this scheme
 // (an infinite x gives lo = NaN); COMPUTE_32F keeps the exact FFMA kernel.
 //
-// Measured against an f64 product (N(0,1) inputs, B200): the normwise error
-// grows linearly with K, about 1.1e-8 * K (6.1e-6 at K = 512, 2.2e-5 at 2048,
-// 8.6e-5 at 8192), while the split itself costs about 1e-6: it is the tensor
-// core's f32 accumulation, which loses a fraction of an ulp toward zero at
-// every accumulate step, so the error tracks the number of steps. The FFMA
-// kernel stays near 1e-6 at any K. Hence the path is taken only up to K = 384
-// (about 4e-6, inside the FP32 tolerance of 1e-5 with margin).
+// Measured against an f64 product (N(0,1) inputs, B200): with one accumulator
+// the normwise error grows linearly with K, about 1.1e-8 * K (6.1e-6 at
+// K = 512, 2.2e-5 at 2048, 8.6e-5 at 8192), while the split itself costs about
+// 1e-6: it is the tensor core's f32 accumulation, which loses a fraction of an
+// ulp toward zero at every accumulate step, so the error tracks the number of
+// steps. The GEMM kernel therefore accumulates its IN_TF32 K loop in fills of
+// 36 stages (1152 elements of the 3K axis, like one K = 384 GEMM: ~4.7e-6) and
+// adds the fills in TMEM with exact f32 adds (gemm_tc_sm100.cu), which keeps
+// the error at the one-fill level for any K.
 #include "gs_internal.h"
 
 namespace gs {
@@ -86,12 +88,11 @@ cudaError_t split(Context &ctx, const float *X, long long ld, long long stride, 
 }  // namespace
 
 // The split costs two extra launches and 4x the operand bytes; below about a
-// GFLOP, or with an output too thin for a 128-row tile, the FFMA kernel is as
-// fast. Past K = 384 the tensor core's accumulation error would exceed the
-// FP32 tolerance (see above).
+// GFLOP, or with an output too thin for a 128-row tile, the FFMA kernel is as fast.
 bool tf32_worthwhile(const GemmDesc &d) {
     const double flops = 2.0 * d.m * d.n * static_cast<double>(d.k) * d.batch;
-    return flops >= 1.0e9 && d.m >= 128 && d.n >= 128 && d.k <= 384;
+    const long long kp = (static_cast<long long>(d.k) + 3) / 4 * 4;
+    return flops >= 1.0e9 && d.m >= 128 && d.n >= 128 && 3 * kp <= 0x7fffffffLL;
 }
 
 cudaError_t launch_tf32(Context &ctx, const GemmDesc &d) {

@@ -414,12 +414,15 @@ def test_fp32_fast_tf32_runs_exact_ffma(handle, op_a, op_b):
     (1, 1, 1024, 1024, 200, 3, (0, 0, 0), False, gs.KERNEL_TC_TF32),   # strided batch
     (0, 0, 1024, 2048, 256, 2, (0, 0, 0), True, gs.KERNEL_TC_TF32),    # broadcast A (stride 0)
     (2, 2, 1100, 1300, 350, 1, (1, 0, 5), False, gs.KERNEL_TC_TF32),   # op C, ragged tiles
-    (0, 0, 1024, 512, 2048, 1, (0, 0, 0), False, gs.KERNEL_FFMA),      # K past the tf32 bound: exact FFMA
+    (0, 0, 1024, 512, 2048, 1, (0, 0, 0), False, gs.KERNEL_TC_TF32),   # 6 accumulator fills
+    (1, 0, 768, 640, 1601, 2, (0, 2, 3), False, gs.KERNEL_TC_TF32),    # 5 fills, the last one partial; batched
+    (0, 1, 128, 4096, 1200, 1, (0, 0, 0), False, gs.KERNEL_TC_TF32),   # M = 128: the 1-SM tile path
+    (0, 0, 100, 512, 4096, 1, (0, 0, 0), False, gs.KERNEL_FFMA),       # output thinner than a 128-row tile
 ])
 def test_fast_tf32_tensor_cores(handle, op_a, op_b, m, n, k, batch, pad, bcast_a, kernel):
-    """COMPUTE_32F_FAST_TF32 on large short-K problems runs tcgen05 kind::tf32 over the split operands (three tf32
-    products per f32 product) and must still meet the FP32 normwise tolerance against the oracle; longer K stays on
-    the exact FFMA kernel."""
+    """COMPUTE_32F_FAST_TF32 on large problems runs tcgen05 kind::tf32 over the split operands (three tf32 products
+    per f32 product; K accumulated in fills of 36 stages that the epilogue adds in TMEM with exact f32 adds) and must
+    still meet the FP32 normwise tolerance against the oracle."""
     run_case(handle, gs.R_32F, op_a, op_b, m, n, k, alpha=1.5, beta=-0.5, pad=pad, batch=batch, bcast_a=bcast_a,
              seed=m + n + k + batch, comp=gs.COMPUTE_32F_FAST_TF32, expect_kernel=kernel)
 
