@@ -64,6 +64,10 @@ CONFIGS = {
     "c5b-i8-strided": dict(api="strided", dt=3, ct=10, comp=72, op=(0, 0), m=2048, n=2048, k=2048, batch=64,
                            alpha=1.0, beta=0.0, shard="batch",
                            label="gemmStridedBatchedEx C5b: s8 -> s32, batch 64, M=N=K=2048"),
+    "c3-f32-fast-tf32": dict(api="ex", dt=0, ct=0, comp=77, op=(0, 0), m=8192, n=8192, k=8192, batch=1, alpha=1.0,
+                             beta=0.0, shard="cols",
+                             label="gemmEx: A,B,C CUDA_R_32F uniform [-1,1), COMPUTE_32F_FAST_TF32 (three tf32 "
+                                   "products per f32 product, FP32 tolerance), op N/N, M=N=K=8192"),
     "c2-sgemm-nn": dict(api="sgemm", dt=0, ct=0, comp=68, op=(0, 0), m=4096, n=1024, k=2048, batch=1, alpha=1.5,
                         beta=0.5, shard="cols", label="sgemm C2: FP32 op N/N, 4096x1024x2048, alpha=1.5, beta=0.5"),
     "c2-sgemm-tt": dict(api="sgemm", dt=0, ct=0, comp=68, op=(1, 1), m=1024, n=4096, k=512, batch=1, alpha=1.5,
@@ -106,6 +110,15 @@ def roofline_of(cfg: dict, flops: float, byts: float, ms_per_launch: float, peak
         return {"bound": "ffma", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic,
                 "peak_source": "nominal 148 SM x 128 FP32 lanes x 2 x max SM clock (no measured FFMA peak)"}
+    if cfg["comp"] == 77:
+        # FAST_TF32: the dense tf32 rate is half the bf16 rate; the kernel runs three tf32 products per f32
+        # product, so `achieved` (algorithmic 2MNK) can reach at most a third of this peak.
+        peak = peaks["bf16"] / 2.0
+        achieved = flops / (ms_per_launch * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": f"{peaks['source']} cuBLAS bf16 burst / 2 (dense tf32); the kernel executes "
+                               "3 tf32 products per f32 product, so hardware work is 3x achieved"}
     tensor_peak = peaks["bf16"] * (2.0 if cfg["dt"] == 3 else 1.0)
     ridge = tensor_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
     if ai < ridge:
