@@ -103,6 +103,9 @@ cudaError_t launch_tf32(Context &ctx, const GemmDesc &d) {
     const size_t b_elems = static_cast<size_t>(batch_b) * d.n * 3 * kp;
     const size_t a_bytes = (a_elems * sizeof(float) + 255) / 256 * 256;
     const size_t need = a_bytes + b_elems * sizeof(float);
+    // The split operands are 3x the f32 operands and stay allocated with the
+    // handle; past 16 GiB the caller's memory matters more than the speed-up.
+    if (need > (static_cast<size_t>(16) << 30)) return cudaErrorMemoryAllocation;
     if (ctx.tf32_bytes < need) {
         if (ctx.tf32_buf) cudaFree(ctx.tf32_buf);
         ctx.tf32_buf = nullptr;
