@@ -3,6 +3,7 @@
 // Computes C = alpha * op(A) * op(B) + beta * C, column-major, for
 //   f16 x f16 -> f32 / f16 and bf16 x bf16 -> f32 / bf16  (tcgen05.mma kind::f16)
 //   s8 x s8 -> s32                                         (tcgen05.mma kind::i8)
+//   split f32 (FAST_TF32, see tf32_split.cu) -> f32          (tcgen05.mma kind::tf32)
 // It replaces slang-gemm's cooperative-matrix shaders
 // (shaders/gemm_nvcoop2_f16.slang, shaders/gemm_nvcoop2_i8.slang and the bf16
 // path of tools/emit_nvcoop2_spv.zig); the arithmetic contract is gemmExCuda
@@ -15,8 +16,11 @@
 //    the wide variant (long K loops) computes 256 x 512 with two such MMAs per
 //    K step into all 512 TMEM columns, cutting operand traffic by another 1/4;
 //    CG = 1: one CTA computes a 128 x 256 tile;
-//  - 128 bytes of K per pipeline stage (64 f16/bf16 or 128 s8), 6 stages (CG 2)
-//    or 4 stages (CG 1 and the wide pair tile);
+//  - 128 bytes of K per pipeline stage (64 f16/bf16, 128 s8 or 32 tf32), 6
+//    stages (CG 2) or 4 stages (CG 1 and the wide pair tile);
+//  - tf32 accumulates its K loop in fills of CHUNK_KB stages that the epilogue
+//    folds into a running sum in the second TMEM half with exact f32 adds (the
+//    tensor core's accumulation loses part of an ulp per step);
 //  - warp 0: TMA producer. Operand transposes live in the tensor maps: op(A)=N
 //    (M-contiguous) and op(B)=T (N-contiguous) are fetched as MN-major 128-byte
 //    swizzled panels, op(A)=T and op(B)=N as K-major panels, and the UMMA
