@@ -2,7 +2,7 @@
 sets kernel attributes and allocates the handle's tensor-map buffer), a call
 captured into a graph and replayed must give the same bits as the direct
 call, for every kernel family (tensor-core single / strided / pointer-array,
-FFMA, CUDA-core fallback, k = 0)."""
+FFMA, the FAST_TF32 split + tf32 GEMM, CUDA-core fallback, k = 0)."""
 import numpy as np
 import pytest
 import torch
@@ -24,6 +24,7 @@ def _dev(x):
     (gs.R_32F, 300, 200, 100, 2, 0, False, -1),     # FFMA sgemm
     (gs.R_16F, 100, 60, 40, 1, 3, False, -1),       # CUDA-core fallback (misaligned leading dimension)
     (gs.R_16F, 64, 64, 0, 1, 0, False, -1),         # k == 0: beta only
+    (gs.R_32F, 1024, 512, 1100, 1, 0, False, -1),   # FAST_TF32: split kernels + chunked kind::tf32 GEMM
 ])
 def test_graph_replay_matches_direct_call(dt, m, n, k, batch, lda_pad, ptr, algo):
     rng = np.random.default_rng(m + n + k)
@@ -45,6 +46,9 @@ def test_graph_replay_matches_direct_call(dt, m, n, k, batch, lda_pad, ptr, algo
                                                dtype=torch.int64, device="cuda")
             return h.gemm_batched_ex(0, 0, m, n, k, alpha, arr(A, sa, es), dt, lda, arr(B, sb, es), dt, ldb, beta,
                                      arr(C, sc, ec), ct, ldc, batch, comp, algo=algo)
+        if dt == gs.R_32F and batch == 1 and k > 1000:
+            return h.gemm_ex(0, 0, m, n, k, alpha, A, dt, lda, B, dt, ldb, beta, C, ct, ldc,
+                             gs.COMPUTE_32F_FAST_TF32)
         if dt == gs.R_32F and batch == 1:
             return h.sgemm(0, 0, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc)
         return h.gemm_strided_batched_ex(0, 0, m, n, k, alpha, A, dt, lda, sa, B, dt, ldb, sb, beta, C, ct, ldc, sc,
