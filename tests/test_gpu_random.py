@@ -107,3 +107,49 @@ def test_random_case(handle, i):
         tol_dt = ct
     assert_parity(got, ref, ct, tol_dt, mask=mask, c_before=c0)
     assert handle.device_error() == 0, c
+
+
+def draw_tf32(i):
+    rng = np.random.default_rng(5000 + i)
+    while True:
+        m, n = int(rng.integers(128, 2049)), int(rng.integers(128, 2049))
+        k = int(np.exp(rng.uniform(np.log(64), np.log(4000))))
+        batch = int(rng.choice([1, 1, 2]))
+        flops = 2.0 * m * n * k * batch
+        if 1.0e9 <= flops <= 4.0e9:
+            break
+    return dict(m=m, n=n, k=k, batch=batch, op_a=int(rng.integers(3)), op_b=int(rng.integers(3)),
+                pads=[int(rng.choice([0, 0, 1, 4])) for _ in range(3)], spads=[int(rng.choice([0, 8])) for _ in range(3)],
+                alpha=float(rng.uniform(-2, 2)), beta=float(rng.choice([0.0, 0.5, -1.0])), seed=int(rng.integers(1 << 30)))
+
+
+@pytest.mark.parametrize("i", range(24))
+def test_random_fast_tf32_case(handle, i):
+    """Seeded sweep of COMPUTE_32F_FAST_TF32 problems large enough for the tensor-core path (split operands, chunked
+    kind::tf32 accumulation): ops, ragged shapes, padded leading dimensions and strides, batches, alpha / beta —
+    each within the FP32 tolerance of the oracle, with C's padding untouched."""
+    c = draw_tf32(i)
+    m, n, k, batch, op_a, op_b = c["m"], c["n"], c["k"], c["batch"], c["op_a"], c["op_b"]
+    rng = np.random.default_rng(c["seed"])
+    ar, ac = (m, k) if op_a == 0 else (k, m)
+    br, bc = (k, n) if op_b == 0 else (n, k)
+    lda, ldb, ldc = ar + c["pads"][0], br + c["pads"][1], m + c["pads"][2]
+    sa, sb, sc = ext(ar, ac, lda) + c["spads"][0], ext(br, bc, ldb) + c["spads"][1], ext(m, n, ldc) + c["spads"][2]
+    a = make_input(rng, sa * batch, gs.R_32F)
+    b = make_input(rng, sb * batch, gs.R_32F)
+    c0 = make_c(rng, sc * batch, gs.R_32F)
+    dc = to_dev(c0)
+    handle.gemm_strided_batched_ex(op_a, op_b, m, n, k, c["alpha"], to_dev(a), gs.R_32F, lda, sa, to_dev(b), gs.R_32F,
+                                   ldb, sb, c["beta"], dc, gs.R_32F, ldc, sc, batch, gs.COMPUTE_32F_FAST_TF32)
+    assert handle.last_kernels() & gs.KERNEL_TC_TF32, c
+    got = to_host(dc)
+    ref = c0.copy()
+    assert orc.gemm_ex(op_a, op_b, m, n, k, c["alpha"], a, gs.R_32F, lda, b, gs.R_32F, ldb, c["beta"], ref, gs.R_32F,
+                       ldc, compute_type=gs.COMPUTE_32F_FAST_TF32, batch=batch, sa=sa, sb=sb, sc=sc,
+                       threads=32) == orc.OK
+    mask = np.zeros(c0.size, dtype=bool)
+    idx = (np.arange(batch)[:, None, None] * sc + np.arange(n)[None, :, None] * ldc +
+           np.arange(m)[None, None, :]).ravel()
+    mask[idx] = True
+    assert_parity(got, ref, gs.R_32F, gs.R_32F, mask=mask, c_before=c0)
+    assert handle.device_error() == 0, c
