@@ -92,7 +92,9 @@ cudaError_t split(Context &ctx, const float *X, long long ld, long long stride, 
 bool tf32_worthwhile(const GemmDesc &d) {
     const double flops = 2.0 * d.m * d.n * static_cast<double>(d.k) * d.batch;
     const long long kp = (static_cast<long long>(d.k) + 3) / 4 * 4;
-    return flops >= 1.0e9 && d.m >= 128 && d.n >= 128 && 3 * kp <= 0x7fffffffLL;
+    // (rows of the split grid: 32 per block, at most 65535 blocks)
+    return flops >= 1.0e9 && d.m >= 128 && d.n >= 128 && 3 * kp <= 0x7fffffffLL && d.m <= 65535 * 32 &&
+           d.n <= 65535 * 32;
 }
 
 cudaError_t launch_tf32(Context &ctx, const GemmDesc &d) {
