@@ -380,6 +380,21 @@ static long long ctas(const GemmDesc &d) {
 cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *a_arr, const void *const *b_arr,
                             void *const *c_arr) {
     using namespace ffma;
+    // Column tiles are grid.y (at most 65535 blocks): wider problems run as
+    // column slices that every tile size can cover (B and C offset per slice).
+    constexpr long long kSliceCols = 65535LL * 32;
+    if (d.n > kSliceCols) {
+        if (a_arr != nullptr) return cudaErrorInvalidValue;  // per-entry pointers cannot be offset here
+        for (long long j0 = 0; j0 < d.n; j0 += kSliceCols) {
+            GemmDesc s = d;
+            s.n = static_cast<int>(d.n - j0 < kSliceCols ? d.n - j0 : kSliceCols);
+            s.B = static_cast<const float *>(d.B) + (d.trans_b ? j0 : j0 * d.ldb);
+            s.C = static_cast<float *>(d.C) + j0 * d.ldc;
+            const cudaError_t e = launch_ffma_ptr(ctx, s, nullptr, nullptr, nullptr);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
     FfmaArgs a{};
     a.a_arr = reinterpret_cast<const float *const *>(a_arr);
     a.b_arr = reinterpret_cast<const float *const *>(b_arr);

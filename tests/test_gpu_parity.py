@@ -236,6 +236,12 @@ def test_sgemm_config1_and_edges(handle):
     sgemm_case(handle, 2, 2, 257, 129, 9, 1.0, 1.0, seed=24)
 
 
+@pytest.mark.parametrize("op_b", [0, 1])
+def test_sgemm_wider_than_one_grid(handle, op_b):
+    """More than 65535 * 32 output columns: the FFMA launcher cuts C (and B) into column slices, each one grid."""
+    sgemm_case(handle, 0, op_b, 8, 2_200_000, 4, 1.25, 0.5, seed=26 + op_b)
+
+
 def test_sgemm_strided_batched(handle):
     rng = np.random.default_rng(25)
     m, n, k, batch = 96, 80, 40, 3
