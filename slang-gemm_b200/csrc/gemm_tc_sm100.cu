@@ -147,9 +147,11 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
     // loses a fraction of an ulp toward zero per accumulate step, so K is
     // accumulated in chunks of CHUNK_KB stages in TMEM columns [0, 256) and the
     // epilogue adds each chunk into a running sum in columns [256, 512) with
-    // exact f32 adds; only the last chunk's sum is stored.
-    constexpr bool CHUNKED = IN == IN_TF32;
-    static_assert(!CHUNKED || !WIDE, "the chunked accumulation needs the second TMEM half");
+    // exact f32 adds; only the last chunk's sum is stored. Problems of a
+    // single fill keep the usual double-buffered accumulators. The wide tile
+    // has no second half to spare: it takes tf32 problems of a single fill only.
+    constexpr bool CHUNKED = IN == IN_TF32 && !WIDE;
+    const bool chunked = CHUNKED && args.k_blocks > CHUNK_KB;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -303,16 +305,16 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
             };
             uint32_t chunks = 0;  // CHUNKED: accumulator fills issued so far
             for (long long t = tile0; ok && t < args.total_tiles; t += tile_step, ++it) {
-                const int acc = (WIDE || CHUNKED) ? 0 : (it & 1);
+                const int acc = (WIDE || chunked) ? 0 : (it & 1);
                 const uint32_t acc_phase = WIDE ? (it & 1) : ((it >> 1) & 1);
-                if constexpr (!CHUNKED) {
+                if (!chunked) {
                     if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, 2)) break;
                     tc_fence_after();
                 }
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 for (int kb = 0; kb < args.k_blocks; ++kb) {
-                    const int kb_in = CHUNKED ? kb % CHUNK_KB : kb;  // stage within the accumulator fill
-                    if (CHUNKED && kb_in == 0) {
+                    const int kb_in = chunked ? kb % CHUNK_KB : kb;  // stage within the accumulator fill
+                    if (chunked && kb_in == 0) {
                         // the epilogue has folded the previous fill into the running sum
                         if (!mbar_wait(&tempty[0], (chunks & 1u) ^ 1u, args.err, 2)) { ok = false; break; }
                         tc_fence_after();
@@ -355,12 +357,12 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     if (!ok) break;
                     commit_to(&empty[stage]);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
-                    if (CHUNKED && (kb_in == CHUNK_KB - 1 || kb + 1 == args.k_blocks)) {
+                    if (chunked && (kb_in == CHUNK_KB - 1 || kb + 1 == args.k_blocks)) {
                         commit_to(&tfull[0]);
                         ++chunks;
                     }
                 }
-                if (ok && !CHUNKED) commit_to(&tfull[WIDE ? 1 : acc]);
+                if (ok && !chunked) commit_to(&tfull[WIDE ? 1 : acc]);
             }
         }
     } else {
@@ -390,7 +392,7 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
             int b, mb, nb;
             tile_coords(args, t, b, mb, nb);
             const int m = mb * C_::TILE_M + static_cast<int>(rank) * BM + row;
-            const int nfills = CHUNKED ? (args.k_blocks + CHUNK_KB - 1) / CHUNK_KB : 1;
+            const int nfills = chunked ? (args.k_blocks + CHUNK_KB - 1) / CHUNK_KB : 1;
             if constexpr (CHUNKED) {
                 // Fold every fill but the last into the running sum (columns BN..2BN-1), in order.
 #pragma unroll 1
@@ -427,8 +429,8 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
             // buffer, or (WIDE) each half of the 512-column accumulator in turn.
 #pragma unroll 1
             for (int half = 0; half < C_::NSUB; ++half) {
-            const int acc = WIDE ? half : (CHUNKED ? 0 : (it & 1));
-            const uint32_t acc_phase = CHUNKED ? (echunks & 1u) : (WIDE ? (it & 1) : ((it >> 1) & 1));
+            const int acc = WIDE ? half : (chunked ? 0 : (it & 1));
+            const uint32_t acc_phase = chunked ? (echunks & 1u) : (WIDE ? (it & 1) : ((it >> 1) & 1));
             if (!mbar_wait(&tfull[acc], acc_phase, args.err, 4)) { ok = false; break; }
             tc_fence_after();
             const int n0 = nb * TILE_N + half * BN;  // tile column of this slot's first accumulator column
@@ -437,7 +439,7 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
             for (int c = c_lo; c < c_lo + C_::EPI_COLS; c += 32) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_lane + acc * BN + c, r);
-                if (CHUNKED && nfills > 1) {
+                if (chunked && nfills > 1) {
                     uint32_t sum[32];
                     tmem_ld_32x32b_x32(t_lane + BN + c, sum);
                     tmem_wait_ld();
@@ -500,7 +502,7 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                 }
             }
             arrive_tempty(acc);
-            if (CHUNKED) ++echunks;
+            if (chunked) ++echunks;
             }  // accumulator slots of this tile
         }
         if (c_tma && lane == 0) bulk_wait_group_all();  // C is written before the kernel ends
@@ -628,10 +630,8 @@ static cudaError_t dispatch(Context &ctx, const GemmDesc &d, const CUtensorMap &
     case IN_I8:
         if (d.out_kind == OUT_I32) return launch_kernel<IN_I8, OUT_I32, CG, WIDE>(ctx, ta, tb, tcm, args);
         break;
-    case IN_TF32:  // chunked accumulation: never the wide tile
-        if constexpr (!WIDE) {
-            if (d.out_kind == OUT_F32) return launch_kernel<IN_TF32, OUT_F32, CG, WIDE>(ctx, ta, tb, tcm, args);
-        }
+    case IN_TF32:  // the wide tile only for a single accumulator fill (choose_shape)
+        if (d.out_kind == OUT_F32) return launch_kernel<IN_TF32, OUT_F32, CG, WIDE>(ctx, ta, tb, tcm, args);
         break;
     default: break;
     }
@@ -747,8 +747,10 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int shape) {
 static int choose_shape_any(const GemmDesc &d);
 static int choose_shape(const Context &, const GemmDesc &d) {
     const int shape = choose_shape_any(d);
-    // TF32 keeps a running sum in the second TMEM half, which the wide tile uses.
-    return shape == 3 && d.in_kind == IN_TF32 ? 2 : shape;
+    // TF32 past one accumulator fill keeps a running sum in the second TMEM
+    // half, which the wide tile occupies.
+    const int k_blocks = (d.k + BK_BYTES / 4 - 1) / (BK_BYTES / 4);
+    return shape == 3 && d.in_kind == IN_TF32 && k_blocks > CHUNK_KB ? 2 : shape;
 }
 static int choose_shape_any(const GemmDesc &d) {
     if (d.algo == 0) return 1;
