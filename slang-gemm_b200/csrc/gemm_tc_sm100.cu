@@ -312,7 +312,58 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     tc_fence_after();
                 }
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < args.k_blocks; ++kb) {
+                // One K step of sub-MMA s from stage st into accumulator columns s*BN..;
+                // `first` starts the accumulation (the first K step of a tile or fill).
+                auto issue = [&](int st, int s, bool first) {
+                    const uint32_t a_base = smem_u32(smA + st * C_::A_STAGE);
+                    const uint32_t b_base = smem_u32(smB + st * C_::B_STAGE + s * C_::B_SUB);
+#pragma unroll
+                    for (int kk = 0; kk < BK / UK; ++kk) {
+                        const uint64_t adesc = args.a_mn
+                                                   ? umma_smem_desc_sw128(a_base + kk * UK * 128, CH_BYTES, 1024)
+                                                   : umma_smem_desc_sw128(a_base + kk * UK * ES, 16, 1024);
+                        const uint64_t bdesc = args.b_mn
+                                                   ? umma_smem_desc_sw128(b_base + kk * UK * 128, CH_BYTES, 1024)
+                                                   : umma_smem_desc_sw128(b_base + kk * UK * ES, 16, 1024);
+                        const uint32_t accum = (!first || kk != 0) ? 1u : 0u;
+                        const uint32_t d = d_tmem + s * BN;
+                        if constexpr (CG == 2) {
+                            if constexpr (IN == IN_I8) umma_i8_2sm(d, adesc, bdesc, idesc, accum);
+                            else if constexpr (IN == IN_TF32) umma_tf32_2sm(d, adesc, bdesc, idesc, accum);
+                            else umma_f16_2sm(d, adesc, bdesc, idesc, accum);
+                        } else {
+                            if constexpr (IN == IN_I8) umma_i8(d, adesc, bdesc, idesc, accum);
+                            else if constexpr (IN == IN_TF32) umma_tf32(d, adesc, bdesc, idesc, accum);
+                            else umma_f16(d, adesc, bdesc, idesc, accum);
+                        }
+                    }
+                };
+                int kb = 0;
+                if constexpr (WIDE) {
+                    // The second accumulator half is drained after the first, so the tile
+                    // opens with the first half's MMAs over the stages already loaded, then
+                    // waits for the second half and catches up on the same stages.
+                    const int P = args.k_blocks < STAGES ? args.k_blocks : STAGES;
+                    int st = stage;
+                    uint32_t ph = phase;
+                    for (int j = 0; j < P; ++j) {
+                        if (!mbar_wait(&full[st], ph, args.err, 3)) { ok = false; break; }
+                        tc_fence_after();
+                        issue(st, 0, j == 0);
+                        if (j + 1 == args.k_blocks) commit_to(&tfull[0]);
+                        if (++st == STAGES) { st = 0; ph ^= 1u; }
+                    }
+                    if (!ok) break;
+                    if (!mbar_wait(&tempty[1], acc_phase ^ 1u, args.err, 2)) break;
+                    tc_fence_after();
+                    for (int j = 0; j < P; ++j) {
+                        issue(stage, 1, j == 0);
+                        commit_to(&empty[stage]);
+                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    }
+                    kb = P;
+                }
+                for (; kb < args.k_blocks; ++kb) {
                     const int kb_in = chunked ? kb % CHUNK_KB : kb;  // stage within the accumulator fill
                     if (chunked && kb_in == 0) {
                         // the epilogue has folded the previous fill into the running sum
@@ -321,40 +372,13 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     }
                     if (!mbar_wait(&full[stage], phase, args.err, 3)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_base = smem_u32(smA + stage * C_::A_STAGE);
 #pragma unroll
                     for (int s = 0; s < C_::NSUB; ++s) {
-                        if (WIDE && s == 1 && kb == 0) {
-                            // The second half of the accumulator may still be draining.
-                            if (!mbar_wait(&tempty[1], acc_phase ^ 1u, args.err, 2)) { ok = false; break; }
-                            tc_fence_after();
-                        }
-                        const uint32_t b_base = smem_u32(smB + stage * C_::B_STAGE + s * C_::B_SUB);
-#pragma unroll
-                        for (int kk = 0; kk < BK / UK; ++kk) {
-                            const uint64_t adesc = args.a_mn
-                                                       ? umma_smem_desc_sw128(a_base + kk * UK * 128, CH_BYTES, 1024)
-                                                       : umma_smem_desc_sw128(a_base + kk * UK * ES, 16, 1024);
-                            const uint64_t bdesc = args.b_mn
-                                                       ? umma_smem_desc_sw128(b_base + kk * UK * 128, CH_BYTES, 1024)
-                                                       : umma_smem_desc_sw128(b_base + kk * UK * ES, 16, 1024);
-                            const uint32_t accum = (kb_in | kk) != 0;
-                            const uint32_t d = d_tmem + s * BN;
-                            if constexpr (CG == 2) {
-                                if constexpr (IN == IN_I8) umma_i8_2sm(d, adesc, bdesc, idesc, accum);
-                                else if constexpr (IN == IN_TF32) umma_tf32_2sm(d, adesc, bdesc, idesc, accum);
-                                else umma_f16_2sm(d, adesc, bdesc, idesc, accum);
-                            } else {
-                                if constexpr (IN == IN_I8) umma_i8(d, adesc, bdesc, idesc, accum);
-                                else if constexpr (IN == IN_TF32) umma_tf32(d, adesc, bdesc, idesc, accum);
-                                else umma_f16(d, adesc, bdesc, idesc, accum);
-                            }
-                        }
+                        issue(stage, s, kb_in == 0);
                         // Last K step: publish the first half as soon as its MMAs are issued,
                         // so its drain overlaps the second half's last MMAs.
                         if (WIDE && s == 0 && kb + 1 == args.k_blocks) commit_to(&tfull[0]);
                     }
-                    if (!ok) break;
                     commit_to(&empty[stage]);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     if (chunked && (kb_in == CHUNK_KB - 1 || kb + 1 == args.k_blocks)) {
