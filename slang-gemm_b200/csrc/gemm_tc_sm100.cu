@@ -780,6 +780,15 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int shape) {
     return a;
 }
 
+// Share of a persistent pair launch's tile slots that hold output: tiles of
+// 256 x tile_n run in rounds of `pairs`, the last round partly idle, edge
+// tiles partly outside C.
+static double slot_use(const GemmDesc &d, int tile_n, long long pairs, long long *rounds) {
+    const long long tiles = static_cast<long long>((d.m + 2 * BM - 1) / (2 * BM)) * ((d.n + tile_n - 1) / tile_n) * d.batch;
+    *rounds = (tiles + pairs - 1) / pairs;
+    return static_cast<double>(d.m) * d.n * d.batch / (static_cast<double>(*rounds) * pairs * 2 * BM * tile_n);
+}
+
 // Tile-shape choice. The algo argument is honoured as a hint
 // (CUBLAS_GEMM_ALGO0 = 1-SM 128 x 256 tile, ALGO1 = 2-SM 256 x 256 pair tile,
 // ALGO2 = 2-SM 256 x 512 wide pair tile); any other value picks the pair tile
@@ -788,19 +797,25 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int shape) {
 // (>= 32 stages) to amortise the undoubled accumulator's drain, or an
 // arithmetic intensity below the B200's tensor / HBM ridge (~260 flop/byte
 // for 16-bit inputs, ~520 op/byte for INT8), where the wide tile's smaller
-// operand traffic is worth more than the drain it exposes. (Measured: the wide
-// tile wins at 8192^3 and 4096^3 and for batch-256 512x512x1024 FP16; the
-// 256 x 256 tile wins for batch-64 2048^3 INT8, whose epilogue is busy 2/3 of
-// the time.)
-static int choose_shape_any(const GemmDesc &d);
-static int choose_shape(const Context &, const GemmDesc &d) {
-    const int shape = choose_shape_any(d);
+// operand traffic is worth more than the drain it exposes. For 16-bit inputs
+// above the ridge with a short K loop the wide tile still wins (1-3 %) once
+// the launch runs at least four rounds of wide tiles over the SM pairs and
+// its last round leaves no more slots idle than the pair tile's (measured:
+// batch-4 4096x4096x1024 FP16 0.122 -> 0.118 ms, batch-9/11/13
+// 2048x2048x1536 0.095/0.116/0.135 -> 0.093/0.113/0.134); where it fills its
+// last round worse (batch-8 2048x2048x1536 FP16 0.085 -> 0.093) the pair tile
+// stays. INT8 keeps the pair tile there: batch-9/11/13 2048^3 ran 3-4 %
+// slower on the wide tile, and batch-64 2048^3 (C5b) measured between 4 %
+// faster and even across boxes.
+static int choose_shape_any(const GemmDesc &d, long long pairs);
+static int choose_shape(const Context &ctx, const GemmDesc &d) {
+    const int shape = choose_shape_any(d, ctx.sm_count >= 2 ? ctx.sm_count / 2 : 1);
     // TF32 past one accumulator fill keeps a running sum in the second TMEM
     // half, which the wide tile occupies.
     const int k_blocks = (d.k + BK_BYTES / 4 - 1) / (BK_BYTES / 4);
     return shape == 3 && d.in_kind == IN_TF32 && k_blocks > CHUNK_KB ? 2 : shape;
 }
-static int choose_shape_any(const GemmDesc &d) {
+static int choose_shape_any(const GemmDesc &d, long long pairs) {
     if (d.algo == 0) return 1;
     if (d.algo == 1) return 2;
     if (d.algo == 2) return 3;
@@ -814,7 +829,12 @@ static int choose_shape_any(const GemmDesc &d) {
     const double bytes = m * k * es + k * n * es + m * n * static_cast<double>(out_elem_size(d.out_kind)) *
                                                         (d.ep.beta_zero ? 1.0 : 2.0);
     const double ridge = d.in_kind == IN_I8 ? 520.0 : 260.0;
-    return flops / bytes < ridge ? 3 : 2;
+    if (flops / bytes < ridge) return 3;
+    if (d.in_kind != IN_F16 && d.in_kind != IN_BF16) return 2;
+    long long rounds_wide = 0, rounds_pair = 0;
+    const double use_wide = slot_use(d, 2 * BN, pairs, &rounds_wide);
+    const double use_pair = slot_use(d, BN, pairs, &rounds_pair);
+    return rounds_wide >= 4 && use_wide >= use_pair - 1e-3 ? 3 : 2;
 }
 
 }  // namespace tc
