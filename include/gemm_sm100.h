@@ -140,7 +140,9 @@ gs_status gs_hgemm(gs_handle handle, int transa, int transb, int m, int n, int k
  *                                      (hi*hi + hi*lo + lo*hi), K accumulated in chunks added in
  *                                      f32, within the FP32 tolerance; smaller ones on FFMA
  * Anything else returns GS_STATUS_NOT_SUPPORTED. INT8 requires k <= 131071 so
- * that the s32 accumulator cannot overflow. */
+ * that the s32 accumulator cannot overflow. For every type a non-empty problem
+ * with m, n or k above 2^31 - 1025 returns GS_STATUS_NOT_SUPPORTED (the
+ * kernels' tile coordinates are 32-bit). */
 gs_status gs_gemm_ex(gs_handle handle, int transa, int transb, int m, int n, int k,
                      const void *alpha, const void *A, int Atype, int lda,
                      const void *B, int Btype, int ldb, const void *beta,

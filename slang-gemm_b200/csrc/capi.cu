@@ -290,6 +290,13 @@ gs_status check_shape_core(int transa, int transb, int m, int n, int k, int lda,
     if (lda < (a_rows > 1 ? a_rows : 1)) { *why = "lda too small"; return GS_STATUS_INVALID_VALUE; }
     if (ldb < (b_rows > 1 ? b_rows : 1)) { *why = "ldb too small"; return GS_STATUS_INVALID_VALUE; }
     if (ldc < (m > 1 ? m : 1)) { *why = "ldc too small"; return GS_STATUS_INVALID_VALUE; }
+    // Row, column and K coordinates inside the kernels are 32-bit and run up
+    // to one tile past the last row, column or K step.
+    constexpr int kMaxDim = 0x7fffffff - 1024;
+    if (m > 0 && n > 0 && batch > 0 && (m > kMaxDim || n > kMaxDim || k > kMaxDim)) {
+        *why = "m, n and k are limited to 2^31 - 1025 (32-bit tile coordinates)";
+        return GS_STATUS_NOT_SUPPORTED;
+    }
     d->trans_a = transa == GS_OP_N ? 0 : 1;
     d->trans_b = transb == GS_OP_N ? 0 : 1;
     d->m = m;

@@ -30,6 +30,10 @@ size_t extent(int layout, size_t ld, size_t rows, size_t cols) {
     return (rows - 1) + (cols - 1) * ld + 1;
 }
 
+// m, n and k the device entry points accept (their kernels' tile coordinates
+// are 32-bit); checked here before anything is staged.
+constexpr size_t kMaxDim = 0x7fffffff - 1024;
+
 // validateByteSliceLen (src/gemm.zig:769-775); `stride` already resolved.
 gs_status check_len(size_t len, size_t es, size_t ext, size_t stride, size_t batch, const char *what, std::string *why) {
     if (ext == 0) return GS_STATUS_SUCCESS;
@@ -133,7 +137,8 @@ extern "C" gs_status gs_host_gemm_ex(gs_handle h, const gs_ex_desc *d) {
     }
     if (d->m == 0 || d->n == 0) return GS_STATUS_SUCCESS;
     const size_t lim = 0x7fffffff;
-    if (d->m > lim || d->n > lim || d->k > lim || d->lda > lim || d->ldb > lim || d->ldc > lim || d->batch_count > lim) {
+    if (d->m > kMaxDim || d->n > kMaxDim || d->k > kMaxDim || d->lda > lim || d->ldb > lim || d->ldc > lim ||
+        d->batch_count > lim) {
         ctx.last_error = "dimension exceeds the 32-bit device API";
         return GS_STATUS_NOT_SUPPORTED;
     }
@@ -413,7 +418,8 @@ extern "C" gs_status gs_host_gemm_batched_ex(gs_handle h, const gs_ptr_batched_d
     gs_status st = GS_STATUS_SUCCESS;
     if (valid > 0 && d->m != 0 && d->n != 0) {
         const size_t lim = 0x7fffffff;
-        if (d->m > lim || d->n > lim || d->k > lim || d->lda > lim || d->ldb > lim || d->ldc > lim || valid > lim) {
+        if (d->m > kMaxDim || d->n > kMaxDim || d->k > kMaxDim || d->lda > lim || d->ldb > lim || d->ldc > lim ||
+            valid > lim) {
             ctx.last_error = "dimension exceeds the 32-bit device API";
             return GS_STATUS_NOT_SUPPORTED;
         }

@@ -128,6 +128,16 @@ def test_plan_validation_statuses():
     big = 131072
     assert plan(at=gs.R_8I, ct=gs.R_32I, comp=gs.COMPUTE_32I, k=big)[0] == gs.STATUS_NOT_SUPPORTED
     assert plan(at=gs.R_8I, ct=gs.R_32I, comp=gs.COMPUTE_32I, k=big - 1 - 15)[0] == 0
+    # 32-bit tile coordinates: m, n, k above 2^31 - 1025 are refused, empty problems stay no-ops
+    top = 2**31 - 1
+    lim = top - 1024
+    assert plan(m=lim + 1, lda=lim + 1, ldc=lim + 1)[0] == gs.STATUS_NOT_SUPPORTED
+    assert plan(m=lim, lda=lim, ldc=lim)[0] == 0
+    assert plan(n=top)[0] == gs.STATUS_NOT_SUPPORTED
+    assert plan(k=lim + 1, ldb=lim + 1)[0] == gs.STATUS_NOT_SUPPORTED
+    assert plan(k=lim, ldb=lim)[0] == 0
+    assert plan(m=top, n=0, lda=top, ldc=top) == (0, 0)
+    assert plan(m=top, lda=top - 1, ldc=top)[0] == gs.STATUS_INVALID_VALUE  # ld errors come first
 
 
 @pytest.mark.parametrize("units,parts,align", [(256, 1, 1), (256, 8, 1), (64, 8, 1), (8192, 3, 256), (10, 4, 1),
