@@ -79,6 +79,11 @@ ELEM = {0: 4, 2: 2, 3: 1, 10: 4, 14: 2}
 DTYPE_NAME = {0: "f32", 2: "f16", 3: "s8", 14: "bf16"}
 
 
+# NVIDIA's dense (non-sparse) B200 figures, for context beside the measured denominators:
+# FP16/BF16 2.25 PFLOP/s, INT8 4.5 POP/s, TF32 1.125 PFLOP/s, HBM3e 7.7 TB/s (HGX).
+DATASHEET = {"tensor16": 2250.0, "tensor8": 4500.0, "tf32": 1125.0, "hbm_gbs": 7700.0}
+
+
 def load_peaks() -> dict:
     """Roofline denominators: MEASURED_PEAKS.json (driver-written) or the pool's fallback."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -110,28 +115,34 @@ def roofline_of(cfg: dict, flops: float, byts: float, ms_per_launch: float, peak
         return {"bound": "ffma", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic,
                 "peak_source": "nominal 148 SM x 128 FP32 lanes x 2 x max SM clock (no measured FFMA peak)"}
+    tsrc = ("profiles/dram_traffic.json: committed ncu capture of this configuration (dram__bytes_read.sum + "
+            "dram__bytes_write.sum per launch), not measured in this run") if traffic is not None else None
     if cfg["comp"] == 77:
         # FAST_TF32: the dense tf32 rate is half the bf16 rate; the kernel runs three tf32 products per f32
         # product, so `achieved` (algorithmic 2MNK) can reach at most a third of this peak.
         peak = peaks["bf16"] / 2.0
         achieved = flops / (ms_per_launch * 1e-3) / 1e12
         return {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": tsrc,
                 "peak_source": f"{peaks['source']} cuBLAS bf16 burst / 2 (dense tf32); the kernel executes "
-                               "3 tf32 products per f32 product, so hardware work is 3x achieved"}
+                               "3 tf32 products per f32 product, so hardware work is 3x achieved",
+                "peak_datasheet": DATASHEET["tf32"], "frac_datasheet": round(achieved / DATASHEET["tf32"], 4)}
     tensor_peak = peaks["bf16"] * (2.0 if cfg["dt"] == 3 else 1.0)
     ridge = tensor_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
     if ai < ridge:
         achieved = byts / (ms_per_launch * 1e-3) / 1e9
         return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
-                "peak_source": f"{peaks['source']} HBM copy bandwidth"}
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic, "traffic_source": tsrc,
+                "peak_source": f"{peaks['source']} HBM copy bandwidth",
+                "peak_datasheet": DATASHEET["hbm_gbs"], "frac_datasheet": round(achieved / DATASHEET["hbm_gbs"], 4)}
     achieved = flops / (ms_per_launch * 1e-3) / 1e12
-    src = f"{peaks['source']} cuBLAS bf16 burst" + (" x2 for INT8 (dense INT8 rate is twice BF16 on B200)"
-                                                    if cfg["dt"] == 3 else "")
+    src = f"{peaks['source']} cuBLAS bf16 burst" + (" x2 for INT8 (dense INT8 rate is twice BF16 on B200; no "
+                                                    "INT8 peak is measured)" if cfg["dt"] == 3 else "")
+    sheet = DATASHEET["tensor8"] if cfg["dt"] == 3 else DATASHEET["tensor16"]
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(tensor_peak, 1),
             "unit": "TOP/s" if cfg["dt"] == 3 else "TFLOP/s", "frac": round(achieved / tensor_peak, 4),
-            "traffic": traffic, "peak_source": src}
+            "traffic": traffic, "traffic_source": tsrc, "peak_source": src,
+            "peak_datasheet": sheet, "frac_datasheet": round(achieved / sheet, 4)}
 
 
 def committed_traffic(name: str):
@@ -148,9 +159,13 @@ def committed_pipe_utilization(name: str):
     ncu summary (profiles/pipe_utilization.json), if any."""
     p = os.path.join(ROOT, "profiles", "pipe_utilization.json")
     try:
-        return json.load(open(p)).get(name)
+        u = json.load(open(p)).get(name)
     except Exception:
         return None
+    if isinstance(u, dict):
+        u = dict(u, source="profiles/pipe_utilization.json: committed ncu capture of this configuration, "
+                           "not measured in this run")
+    return u
 
 
 # ---- clock sampling during the timed region --------------------------------
@@ -164,6 +179,7 @@ class ClockSampler:
 
     def __init__(self, device_index: int):
         self.samples: list[int] = []
+        self.busy: list[int] = []
         self.reasons = 0
         self.max_mhz = None
         self._stop = threading.Event()
@@ -191,6 +207,7 @@ class ClockSampler:
         try:
             self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
             self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            self.busy.append(nv.nvmlDeviceGetUtilizationRates(self._h).gpu)
         except Exception:
             pass
 
@@ -207,8 +224,10 @@ class ClockSampler:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
         s = sorted(self.samples)
+        b = sorted(self.busy)
         names = [v for bit, v in self.REASONS.items() if self.reasons & bit and bit != 0x1]
-        return {"sm_mhz": s[len(s) // 2], "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(s)}
+        return {"sm_mhz": s[len(s) // 2], "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(s),
+                "gpu_busy_pct": b[len(b) // 2] if b else None}
 
 
 # ---- distributed plumbing -----------------------------------------------------
@@ -226,6 +245,13 @@ def dist_setup(n_gpus: int):
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
+    # Bring the communicator up now and say how many ranks it spans (the log shows every rank's count).
+    t = torch.ones(1, device="cuda")
+    dist.all_reduce(t)
+    torch.cuda.synchronize()
+    print(f"[bench] rank {dist.get_rank()}: NCCL communicator up, nranks={int(t.item())} "
+          f"(world_size {dist.get_world_size()}, NCCL {'.'.join(map(str, torch.cuda.nccl.version()))})",
+          file=sys.stderr, flush=True)
     return dist.get_rank(), dist.get_world_size(), local, dist
 
 
@@ -237,6 +263,18 @@ def max_over_ranks(dist, value: float) -> float:
     t = torch.tensor([value], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def all_ranks(dist, values: list) -> list:
+    """Every rank's `values` (floats), in rank order; [values] without a process group."""
+    if dist is None:
+        return [list(values)]
+    import torch
+
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device="cuda")
+    out = torch.empty(t.numel() * dist.get_world_size(), dtype=torch.float64, device="cuda")
+    dist.all_gather_into_tensor(out, t)
+    return out.view(dist.get_world_size(), -1).tolist()
 
 
 def sum_over_ranks(dist, value: float) -> float:
@@ -333,17 +371,48 @@ def l2_flush_needed(cfg: dict) -> bool:
     return largest <= 126 * 2 ** 20
 
 
-def run_ours(args, cfg_name: str) -> None:
+def config_dict(cfg0: dict, cfg: dict, world: int, scaling: str, shard_of: int = 0) -> dict:
+    """The `config` object of a result line; both arms print the same one for the same workload."""
+    parts = world if world > 1 else shard_of
+    d = {"workload": cfg0["label"], "name": cfg0["name"],
+         "per_rank": {"m": cfg["m"], "n": cfg["n"], "k": cfg["k"], "batch": cfg["batch"]},
+         "sharding": "none" if parts <= 1 else (f"{cfg0['shard']} split, {scaling} scaling, "
+                                                "no data-path collective"),
+         "l2": "flushed (256 MiB write) before every step" if l2_flush_needed(cfg)
+         else "inputs larger than L2 (126 MB)"}
+    if shard_of > 1 and world == 1:
+        d["emulated_shard"] = f"rank 0's share of a {shard_of}-way {scaling} split, run alone on one GPU"
+    return d
+
+
+def run_ours(args, items: list) -> None:
+    """Our arm: every (configuration, scaling) item in one process group, one JSON line per item."""
     import torch
 
     import gemm_sm100 as gs
 
-    cfg0 = dict(CONFIGS[cfg_name], algo=args.algo)
     rank, world, local, dist = dist_setup(args.gpus)
-    cfg, shard = rank_share(cfg0, rank, world, args.scaling)
     peaks = load_peaks()
     stream = torch.cuda.current_stream()
     h = gs.Handle(stream=stream)
+    try:
+        for cfg_name, scaling in items:
+            line = run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name, scaling)
+            if rank == 0:
+                emit(line)
+            torch.cuda.empty_cache()
+    finally:
+        h.close()
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str, scaling: str) -> dict:
+    import torch
+
+    cfg0 = dict(CONFIGS[cfg_name], algo=args.algo, name=cfg_name)
+    parts = world if world > 1 else max(1, args.shard_of)
+    cfg, shard = rank_share(cfg0, rank, parts, scaling)
     A, B, C = make_inputs(cfg, seed=1234 + rank)
     flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device="cuda") if l2_flush_needed(cfg) else None
 
@@ -359,7 +428,6 @@ def run_ours(args, cfg_name: str) -> None:
     launches0 = h.launch_count()
     sampler.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kernel_ms = 0.0
     if flush is None:
         ev0.record(stream)
         for _ in range(args.steps):
@@ -385,6 +453,7 @@ def run_ours(args, cfg_name: str) -> None:
     launches = h.launch_count() - launches0
     dev_err = h.device_error()
     barrier(dist)
+    per_rank = all_ranks(dist, [kernel_ms, clocks.get("gpu_busy_pct") or -1.0, clocks.get("sm_mhz") or -1.0])
     max_elapsed = max_over_ranks(dist, elapsed)
     max_kernel_ms = max_over_ranks(dist, kernel_ms)
     flops_rank, bytes_rank = work(cfg)
@@ -408,8 +477,7 @@ def run_ours(args, cfg_name: str) -> None:
     e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1)) / e2e_steps
     e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
     h2d = A.numel() * A.element_size() + B.numel() * B.element_size()
-    c_dense = True
-    if cfg["beta"] != 0 or not c_dense:
+    if cfg["beta"] != 0:
         h2d += C.numel() * C.element_size()
     d2h = C.numel() * C.element_size()
 
@@ -424,16 +492,11 @@ def run_ours(args, cfg_name: str) -> None:
         "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True,
-        "scaling": "weak" if world > 1 and args.scaling == "weak" else ("strong" if world > 1 else "weak"),
+        "scaling": scaling if world > 1 else "weak",
         "vs_baseline": None,
         "dtype": DTYPE_NAME[cfg["dt"]],
         "data": "synthetic (seeded torch generator; value distributions of the configuration)",
-        "config": {"workload": cfg0["label"], "name": cfg_name,
-                   "per_rank": {"m": cfg["m"], "n": cfg["n"], "k": cfg["k"], "batch": cfg["batch"]},
-                   "sharding": "none" if world == 1 else (f"{cfg0['shard']} split, {args.scaling} scaling, "
-                                                          "no data-path collective"),
-                   "l2": "flushed (256 MiB write) before every step" if flush is not None
-                   else "inputs larger than L2 (126 MB)"},
+        "config": config_dict(cfg0, cfg, world, scaling, 0 if world > 1 else args.shard_of),
         "e2e": {"value": round(e2e_value, 2), "unit": unit, "h2d_bytes_per_step": h2d * world,
                 "d2h_bytes_per_step": d2h * world, "ms_per_step": round(e2e_ms, 3),
                 "path": "gs_host_gemm_ex (pinned host buffers; H2D, kernel, D2H, stream sync per step)"},
@@ -444,6 +507,15 @@ def run_ours(args, cfg_name: str) -> None:
         "device_error_word": dev_err,
         "kernels": h.last_kernels(),
     }
+    if world > 1:
+        import torch.distributed as tdist
+
+        line["ranks"] = {"kernel_ms": [round(r[0], 4) for r in per_rank],
+                         "gpu_busy_pct": [r[1] if r[1] >= 0 else None for r in per_rank],
+                         "sm_mhz": [r[2] if r[2] >= 0 else None for r in per_rank],
+                         "units": [shard.cuts[g + 1] - shard.cuts[g] for g in range(world)],
+                         "unit": "columns" if cfg0["shard"] == "cols" else "batch entries"}
+        line["nccl"] = {"nranks": tdist.get_world_size(), "version": ".".join(map(str, torch.cuda.nccl.version()))}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg0, budget_s=args.cpu_seconds)
     if args.gather and dist is not None:
@@ -451,27 +523,26 @@ def run_ours(args, cfg_name: str) -> None:
         # (not part of `value`: the sharded GEMM itself needs no collective).
         import sharding
 
-        unit = cfg["m"] if cfg0["shard"] == "cols" else cfg["m"] * cfg["n"]
-        sharding.gather_blocks(C, shard, unit)  # warm the communicator
+        unit_elems = cfg["m"] if cfg0["shard"] == "cols" else cfg["m"] * cfg["n"]
+        sharding.gather_blocks(C, shard, unit_elems)  # warm the communicator
         barrier(dist)
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
-        full = sharding.gather_blocks(C, shard, unit)
+        full = sharding.gather_blocks(C, shard, unit_elems)
         g1.record(stream)
         torch.cuda.synchronize()
-        line["allgather"] = {"ms": round(max_over_ranks(dist, g0.elapsed_time(g1)), 3),
-                             "bytes_per_rank": int(full.numel() * full.element_size()), "backend": "nccl"}
+        gms = max_over_ranks(dist, g0.elapsed_time(g1))
+        nbytes = int(full.numel() * full.element_size())
+        line["allgather"] = {"ms": round(gms, 3), "bytes_per_rank": nbytes, "backend": "nccl",
+                             "algbw_gbs": round(nbytes * (world - 1) / world / (gms * 1e-3) / 1e9, 1)}
         del full
     if args.cublas and rank == 0:
         line["cublas"] = cublas_compare(cfg, A, B, args.steps, args.warmup)
         if "ms" in line["cublas"]:
             # the reference's shader_cublas_ratio (bench/gemm_perf.zig:206): our ms / cuBLAS ms, same rank-0 shard
             line["shader_cublas_ratio"] = round(max_kernel_ms / line["cublas"]["ms"], 4)
-    h.close()
-    if dist is not None:
-        dist.destroy_process_group()
-    if rank == 0:
-        emit(line)
+    del A, B, C, flush
+    return line
 
 
 def cublas_compare(cfg: dict, A, B, steps: int, warmup: int) -> dict:
@@ -647,8 +718,32 @@ def _cpu_plan(cfg: dict, threads: int, budget_s: float) -> tuple[int, float]:
     return threads * per, t1
 
 
+def cpu_single_thread(cfg: dict) -> dict:
+    """Single-thread scalar figures of the oracle's loop: (i) the whole GEMM at the reference bench's capped
+    size (min(dim, 256) for classic sgemm, min(dim, 128) for gemmEx; bench/gemm_perf.zig:317-336, :618-637),
+    as the reference times its scalar column; (ii) the full-size GEMM when it is small enough (C1's 512^3),
+    otherwise a two-column sample of it."""
+    cap = 256 if cfg["api"] == "sgemm" else 128
+    small = dict(cfg, m=min(cfg["m"], cap), n=min(cfg["n"], cap), k=min(cfg["k"], cap), batch=1)
+    secs_cap = _cpu_sample(small, small["n"], 1)
+    full = cfg["m"] * cfg["n"] * cfg["k"] <= 2 ** 28
+    cols = cfg["n"] if full else 2
+    secs = _cpu_sample(cfg, cols, 1)
+    unit = "TOP/s" if cfg["dt"] == 3 else "TFLOP/s"
+    f_cap = 2.0 * small["m"] * small["n"] * small["k"]
+    f_full = 2.0 * cfg["m"] * cols * cfg["k"]
+    return {"value": f_full / secs / 1e12, "unit": unit, "cores": 1,
+            "sample": (f"the whole {cfg['m']}x{cfg['n']}x{cfg['k']} GEMM" if full else
+                       f"{cols} of {cfg['n']} output columns of the {cfg['m']}x{cfg['n']}x{cfg['k']} GEMM")
+            + f", {secs:.2f} s",
+            "ms_full_gemm_estimate": round(secs * 1e3 * cfg["n"] / cols * cfg["batch"], 1),
+            "at_reference_cap": {"m": small["m"], "n": small["n"], "k": small["k"], "ms": round(secs_cap * 1e3, 3),
+                                 "value": f_cap / secs_cap / 1e12, "unit": unit}}
+
+
 def cpu_baseline(cfg: dict, budget_s: float = 12.0) -> dict:
-    """The C restatement of the reference's scalar gemmExCuda (src/gemm.zig:671-706), all host cores."""
+    """The C restatement of the reference's scalar gemmExCuda (src/gemm.zig:671-706), all host cores, plus the
+    single-thread scalar figures beside it."""
     threads = os.cpu_count() or 1
     cols, _ = _cpu_plan(cfg, threads, budget_s)
     cols = min(cols, cfg["n"])
@@ -658,14 +753,23 @@ def cpu_baseline(cfg: dict, budget_s: float = 12.0) -> dict:
     return {"value": flops / secs / 1e12, "unit": unit, "cores": threads, "kind": "port",
             "sample": f"{cols} of {cfg['n']} output columns (all {cfg['m']} rows, full K={cfg['k']}) of one "
                       f"{cfg['m']}x{cfg['n']}x{cfg['k']} GEMM, {secs:.1f} s, {threads} threads "
-                      "(oracle/gemm_oracle.c, the scalar f64-accumulating loop of src/gemm.zig)"}
+                      "(oracle/gemm_oracle.c, the scalar f64-accumulating loop of src/gemm.zig)",
+            "single_thread": cpu_single_thread(cfg)}
 
 
-def run_reference(args, cfg_name: str) -> None:
+def rank0_units(units: int, parts: int, align: int) -> int:
+    """Rank 0's share under gs_plan_shards's cut rule (floor(units * g / parts) rounded down to `align`)."""
+    if parts <= 1:
+        return units
+    return (units // parts) // align * align
+
+
+def run_reference(args, cfg_name: str, scaling: str = "weak") -> None:
     """--impl reference: the reference's CPU algorithm on this host, same config / metric / unit."""
     if int(os.environ.get("RANK", "0")) != 0:
         return  # only rank 0 runs and prints under torchrun
-    cfg = CONFIGS[cfg_name]
+    cfg = dict(CONFIGS[cfg_name], name=cfg_name)
+    world = int(os.environ.get("WORLD_SIZE", "1")) if "RANK" in os.environ else 1
     threads = os.cpu_count() or 1
     total_steps = args.steps + args.warmup
     per_step_budget = max(0.5, args.ref_seconds / max(1, total_steps))
@@ -679,15 +783,29 @@ def run_reference(args, cfg_name: str) -> None:
     flops = 2.0 * cfg["m"] * cols * cfg["k"] * args.steps
     value = flops / t / 1e12
     unit = "TOP/s" if cfg["dt"] == 3 else "TFLOP/s"
+    frac = cols / cfg["n"]
     sample = (f"{cols} of {cfg['n']} output columns per step (all {cfg['m']} rows, full K={cfg['k']}), "
               f"{threads} threads, oracle/gemm_oracle.c (C restatement of src/gemm.zig gemmExCuda; "
               "the Zig reference itself cannot be built here)")
+    # Same `config` object as our arm prints for this workload (rank 0's share when N > 1), computed here
+    # without loading libgemm_sm100: this arm runs none of this repository's GPU code.
+    rcfg = dict(cfg)
+    if world > 1:
+        key, align = ("batch", 1) if cfg["shard"] == "batch" else ("n", 256)
+        total = cfg[key] * (world if scaling == "weak" else 1)
+        rcfg[key] = rank0_units(total, world, align)
+    # ms_per_step describes the same work as `value`: one whole step of the configuration (per batch entry
+    # count and full N), extrapolated from the timed column sample at the sampled rate.
+    ms_full = 1000.0 * t / max(1, args.steps) / frac * cfg["batch"]
     line = {
         "metric": METRIC, "value": value, "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1000.0 * t / max(1, args.steps), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_NAME[cfg["dt"]], "data": "synthetic",
-        "config": {"workload": cfg["label"], "name": cfg_name},
+        "warmup": args.warmup, "ms_per_step": round(ms_full, 1), "higher_is_better": True,
+        "scaling": scaling if world > 1 else "weak", "vs_baseline": None, "dtype": DTYPE_NAME[cfg["dt"]],
+        "data": "synthetic (seeded numpy generator; value distributions of the configuration)",
+        "config": config_dict(cfg, rcfg, world, scaling),
         "impl": "reference",
+        "sample_fraction": round(frac * (1.0 / cfg["batch"]), 6),
+        "ms_per_sample": round(1000.0 * t / max(1, args.steps), 1),
         "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -811,9 +929,16 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c3-f16-nn", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c3-f16-nn",
+                    help="configuration name, or a comma-separated list (one JSON line each): "
+                         + ", ".join(sorted(CONFIGS)))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--scaling", default="weak",
+                    help="N > 1: 'weak' (each rank holds one configuration's work), 'strong' (the ranks split one "
+                         "configuration), or 'weak,strong' (both, one line each)")
+    ap.add_argument("--shard-of", type=int, default=0, metavar="N",
+                    help="one GPU runs rank 0's share of an N-way split alone (the per-rank workload of an N-GPU "
+                         "run, for single-GPU profiling)")
     ap.add_argument("--no-cublas", dest="cublas", action="store_false",
                     help="skip timing cuBLAS on the same operands (shader_cublas_ratio)")
     ap.add_argument("--cublas", dest="cublas", action="store_true", help=argparse.SUPPRESS)
@@ -842,6 +967,12 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    names = [c.strip() for c in args.config.split(",") if c.strip()]
+    scalings = [s.strip() for s in args.scaling.split(",") if s.strip()]
+    bad = [c for c in names if c not in CONFIGS] + [s for s in scalings if s not in ("weak", "strong")]
+    if bad or not names or not scalings:
+        ap.error(f"unknown --config / --scaling value(s): {bad}")
+    args.config = names[0]
     row_mode = any(v is not None for v in (args.manifest, args.sizes, args.rect_sizes)) or args.fail_every_row or \
         args.fail_on_regression or args.only_cublas_supported or args.tile_compatible_only
     if row_mode:
@@ -850,9 +981,9 @@ def main():
         run_sustained(args, args.config)
         return
     if args.impl == "reference":
-        run_reference(args, args.config)
+        run_reference(args, args.config, scalings[0])
     else:
-        run_ours(args, args.config)
+        run_ours(args, [(c, s) for c in names for s in scalings])
 
 
 if __name__ == "__main__":

@@ -74,6 +74,16 @@ typedef struct gs_context *gs_handle;
 /* Handle management. Replaces cublas.Context (src/cublas.zig:78-90).      */
 /* ---------------------------------------------------------------------- */
 
+/* Makes current the first CUDA device whose name contains name_substr (any
+ * device when it is NULL or empty) and stores its index in *device. Replaces
+ * the device choice of src/vulkan_runner.zig:1273-1299 (selectPhysicalDevice,
+ * first device whose name contains the --device-substr needle). Statuses:
+ * GS_STATUS_NOT_INITIALIZED when there is no CUDA device at all (the reference's
+ * error.NoVulkanDevice), GS_STATUS_INVALID_VALUE when no name matches
+ * (error.NoMatchingDevice), GS_STATUS_ARCH_MISMATCH when the matching devices
+ * are not compute capability 10.0. Host only: allocates nothing. */
+gs_status gs_select_device(const char *name_substr, int *device);
+
 /* Creates a handle bound to the current CUDA device and the default stream.
  * Returns GS_STATUS_ARCH_MISMATCH when the device is not compute capability 10.0. */
 gs_status gs_create(gs_handle *handle);

@@ -117,6 +117,34 @@ const char *gs_status_name(gs_status s) {
     return "GS_STATUS_UNKNOWN";
 }
 
+gs_status gs_select_device(const char *name_substr, int *device) {
+    if (!device) return GS_STATUS_INVALID_VALUE;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) {
+        cudaGetLastError();
+        return GS_STATUS_NOT_INITIALIZED;
+    }
+    const bool any = name_substr == nullptr || name_substr[0] == '\0';
+    bool matched = false;
+    for (int d = 0; d < count; ++d) {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, d) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        if (!any && std::strstr(prop.name, name_substr) == nullptr) continue;
+        matched = true;
+        if (prop.major != 10 || prop.minor != 0) continue;  // a later match may still be an sm_100 device
+        if (cudaSetDevice(d) != cudaSuccess) {
+            cudaGetLastError();
+            return GS_STATUS_NOT_INITIALIZED;
+        }
+        *device = d;
+        return GS_STATUS_SUCCESS;
+    }
+    return matched ? GS_STATUS_ARCH_MISMATCH : GS_STATUS_INVALID_VALUE;
+}
+
 gs_status gs_create(gs_handle *handle) {
     if (!handle) return GS_STATUS_INVALID_VALUE;
     *handle = nullptr;

@@ -108,6 +108,7 @@ def _load() -> ctypes.CDLL:
     vp, i, ll, u32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_uint32
     st = ctypes.c_int
     sig = {
+        "gs_select_device": (st, [ctypes.c_char_p, ctypes.POINTER(i)]),
         "gs_create": (st, [ctypes.POINTER(vp)]),
         "gs_destroy": (st, [vp]),
         "gs_set_stream": (st, [vp, vp]),
@@ -166,6 +167,14 @@ def declared_symbols(header: str = HEADER_PATH) -> list[str]:
 
     text = open(header).read()
     return sorted(set(re.findall(r"\b(gs_[a-z0-9_]+)\s*\(", text)))
+
+
+def select_device(name_substr: str | None = None) -> tuple[int, int]:
+    """gs_select_device: (status, device index) of the first CUDA device whose name contains `name_substr`
+    (made current), as the reference picks its device by name substring (src/vulkan_runner.zig:1273-1299)."""
+    dev = ctypes.c_int(-1)
+    s = _lib.gs_select_device(name_substr.encode() if name_substr else None, ctypes.byref(dev))
+    return s, dev.value
 
 
 def plan_shards(units: int, parts: int, align: int = 1) -> list[int]:

@@ -93,3 +93,48 @@ def test_cli_reference_arm_prints_one_json_line():
 def test_cli_rejects_short_warmup():
     p = _run("--warmup", "2")
     assert p.returncode != 0
+
+
+@pytest.mark.parametrize("units,parts,align", [(8192, 2, 256), (8192, 8, 256), (65536, 8, 256), (256, 8, 1),
+                                               (64, 8, 1), (512, 4, 1), (1000, 3, 256), (100, 8, 256)])
+def test_reference_arm_rank0_share_matches_the_library_plan(units, parts, align):
+    import gemm_sm100 as gs
+
+    assert bench.rank0_units(units, parts, align) == gs.plan_shards(units, parts, align)[1]
+
+
+@pytest.mark.parametrize("name", ["c3-f16-nn", "c4-f16-strided", "c5b-i8-strided"])
+@pytest.mark.parametrize("world,scaling", [(1, "weak"), (2, "weak"), (8, "strong")])
+def test_both_arms_print_the_same_config_object(name, world, scaling):
+    cfg0 = dict(bench.CONFIGS[name], name=name)
+    ours, _ = bench.rank_share(cfg0, 0, world, scaling)
+    theirs = dict(cfg0)
+    key, align = ("batch", 1) if cfg0["shard"] == "batch" else ("n", 256)
+    theirs[key] = bench.rank0_units(cfg0[key] * (world if scaling == "weak" else 1), world, align)
+    assert bench.config_dict(cfg0, ours, world, scaling) == bench.config_dict(cfg0, theirs, world, scaling)
+
+
+def test_roofline_carries_both_denominators():
+    for name in ("c3-f16-nn", "c5-i8-nn", "c4-f16-strided"):
+        cfg = bench.CONFIGS[name]
+        flops, byts = bench.work(cfg)
+        r = bench.roofline_of(cfg, flops, byts, 1.0, PEAKS, 123)
+        assert r["peak_datasheet"] in (2250.0, 4500.0, 7700.0)
+        assert abs(r["frac_datasheet"] - r["achieved"] / r["peak_datasheet"]) < 1e-3
+        assert "not measured in this run" in r["traffic_source"]
+
+
+def test_reference_arm_line_describes_one_whole_step():
+    p = _run("--impl", "reference", "--config", "c5b-i8-strided", "--steps", "3", "--warmup", "3",
+             "--ref-seconds", "1.5")
+    assert p.returncode == 0, p.stderr[-2000:]
+    d = json.loads(p.stdout.strip().splitlines()[-1])
+    assert 0 < d["sample_fraction"] < 1
+    # ms_per_step is the whole configuration's step: the sample time scaled by 1 / sample_fraction
+    assert d["ms_per_step"] == pytest.approx(d["ms_per_sample"] / d["sample_fraction"], rel=1e-2)
+    assert d["config"]["name"] == "c5b-i8-strided" and d["config"]["per_rank"]["batch"] == 64
+
+
+def test_cli_rejects_unknown_config_in_a_list():
+    p = _run("--config", "c3-f16-nn,nope")
+    assert p.returncode != 0 and "nope" in p.stderr
