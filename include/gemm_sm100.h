@@ -103,6 +103,21 @@ uint64_t gs_launch_count(gs_handle handle);
  * kernels' bounded waits write (0 = no error; bit 0 = a pipeline wait timed
  * out, bits 8..15 = where). The word is sticky for the handle's lifetime. */
 gs_status gs_device_error(gs_handle handle, uint32_t *word);
+/* Limit, in SM clock cycles, of every bounded wait inside this handle's
+ * tensor-core kernels (default 4e9, about 2 s at the B200's top clock; a value
+ * <= 0 restores the default). A wait that runs out records bit 0 and its site
+ * in the device error word and ends the kernel early, with its in-flight copies
+ * and MMAs drained and its tensor memory freed, instead of hanging the GPU: the
+ * bounded counterpart of the reference's fence wait with no time limit
+ * (src/vulkan_runner.zig:2197). Affects calls issued afterwards. */
+gs_status gs_set_wait_limit(gs_handle handle, long long cycles);
+/* Test hook for that failure path: with kblock >= 0 the tensor-core kernel's
+ * TMA producer leaves K block `kblock` of its first tile unfilled (no
+ * expect_tx, no copy) and issues nothing after it, so the MMA issuer's wait for
+ * that stage runs out after the wait limit with no load left in flight. The
+ * call's C is then incomplete and gs_device_error reports the timeout. -1 (the
+ * default) turns it off. No counterpart in the reference. */
+gs_status gs_debug_skip_kblock(gs_handle handle, int kblock);
 
 enum {
     GS_KERNEL_TC_F16 = 1u << 0,   /* tcgen05 kind::f16, f16 operands */
@@ -195,19 +210,31 @@ gs_status gs_plan_gemm_strided_batched_ex(int transa, int transb, int m, int n, 
  * latency-critical path that must not pay the device-wide synchronisation
  * cudaMalloc/cudaFree can imply. Same arguments, types, semantics and status
  * codes as gs_gemm_batched_ex, plus the stream (a cudaStream_t) to run on.
- * Its scratch (per-batch tensor maps and two status words, about 64 KiB) is a
- * static device array in the library that every GPU loading the library holds
- * until the process exits. Limit: batchCount <= GS_NOALLOC_MAX_BATCH;
+ * Its scratch (per-batch tensor maps and status words: 3 * GS_NOALLOC_MAX_BATCH
+ * * 128 + 256 = 98,560 bytes) is a static device array in the library that
+ * every GPU loading the library holds until the process exits. Limit: batchCount <= GS_NOALLOC_MAX_BATCH;
  * larger batches return GS_STATUS_INVALID_VALUE and launch nothing.
  * The first call on a device resolves the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call
  * before any stream capture. All calls share the array and each clears the
  * words that must start at zero, so calls that overlap on the GPU (other
- * streams or host threads) race: order them on one stream. */
+ * streams or host threads) race: order them on one stream. The array's address
+ * is resolved once per device, so do not use this entry point on a device
+ * after cudaDeviceReset in the same process. */
 gs_status gs_gemm_batched_ex_noalloc(void *stream, int transa, int transb, int m, int n, int k, const void *alpha,
                                      const void *const Aarray[], int Atype, int lda, const void *const Barray[],
                                      int Btype, int ldb, const void *beta, void *const Carray[], int Ctype, int ldc,
                                      int batchCount, int computeType);
+
+/* Reads the device error word of the last gs_gemm_batched_ex_noalloc call on
+ * the current device, after synchronising `stream` (the stream that call ran
+ * on): 0 = no error; bit 0 = a pipeline wait in the kernel gave up, bits 8..15
+ * = where (the word gs_device_error reads for a handle). The call returned
+ * success before the kernel ran, so this is how such a caller learns that a
+ * kernel ended early and C is incomplete. Valid until the next no-allocation
+ * call on the device clears it. No counterpart in the reference; allocates
+ * nothing. */
+gs_status gs_noalloc_device_error(void *stream, uint32_t *word);
 
 /* ---------------------------------------------------------------------- */
 /* Host-buffer mirror of gemm.gemmEx                                       */

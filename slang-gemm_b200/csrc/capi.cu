@@ -187,6 +187,7 @@ gs_status gs_destroy(gs_handle h) {
     if (h->ctx.dev_err) cudaFree(h->ctx.dev_err);
     if (h->ctx.stage) cudaFree(h->ctx.stage);
     if (h->ctx.tmap_buf) cudaFree(h->ctx.tmap_buf);
+    for (void *p : h->ctx.retired) cudaFree(p);
     if (h->ctx.tf32_buf) cudaFree(h->ctx.tf32_buf);
     if (h->ctx.h2d) cudaStreamDestroy(h->ctx.h2d);
     if (h->ctx.d2h) cudaStreamDestroy(h->ctx.d2h);
@@ -386,6 +387,19 @@ gs_status run(gs_handle h, GemmDesc &d) {
 }  // namespace gs
 
 extern "C" {
+
+gs_status gs_set_wait_limit(gs_handle h, long long cycles) {
+    if (!h) return GS_STATUS_NOT_INITIALIZED;
+    h->ctx.spin_limit = cycles > 0 ? cycles : gs::kDefaultWaitLimitCycles;
+    return GS_STATUS_SUCCESS;
+}
+
+gs_status gs_debug_skip_kblock(gs_handle h, int kblock) {
+    if (!h) return GS_STATUS_NOT_INITIALIZED;
+    if (kblock < -1) return GS_STATUS_INVALID_VALUE;
+    h->ctx.debug_skip_kb = kblock;
+    return GS_STATUS_SUCCESS;
+}
 
 gs_status gs_device_error(gs_handle h, uint32_t *word) {
     if (!h) return GS_STATUS_NOT_INITIALIZED;

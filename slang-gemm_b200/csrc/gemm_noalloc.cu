@@ -10,12 +10,16 @@
 // neither: the per-batch tensor maps, the misalignment flag and the device
 // error word live in the file-scope array below, sized for at most
 // GS_NOALLOC_MAX_BATCH batch entries. Every GPU that loads the library holds
-// that array (about 64 KiB) until the process exits.
+// that array (3 * 256 tensor maps of 128 bytes plus 256 bytes of status words,
+// 98,560 bytes) until the process exits.
 //
 // The array is shared by every call on a device and keeps the last call's
 // contents; each call clears the words that must start at zero. Calls whose
 // work overlaps on the GPU (different streams, or different host threads)
-// race on the array: order them on one stream.
+// race on the array: order them on one stream. The array's device address is
+// resolved once per device and kept for the life of the process, so the entry
+// point must not be used on a device after cudaDeviceReset in that process
+// (the reset unloads the module that holds the array).
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -28,6 +32,8 @@ constexpr int kMaxBatch = GS_NOALLOC_MAX_BATCH;
 constexpr size_t kMapBytes = 3ull * kMaxBatch * sizeof(CUtensorMap);  // A maps, B maps, C maps
 constexpr size_t kWordBytes = 256;                                     // [0] error word, [1] / [2] misaligned flags
 constexpr size_t kScratchBytes = kMapBytes + kWordBytes;
+static_assert(sizeof(CUtensorMap) == 128 && kScratchBytes == 98560,
+              "the size quoted in the comments and in include/gemm_sm100.h");
 
 // Device scratch of the no-allocation path. In host code this name is only a
 // stand-in for the symbol, never a device address: the kernels receive the
@@ -126,6 +132,27 @@ extern "C" gs_status gs_gemm_batched_ex_noalloc(void *stream, int transa, int tr
         }
     }
     if (e != cudaSuccess) {
+        cudaGetLastError();
+        return GS_STATUS_EXECUTION_FAILED;
+    }
+    return GS_STATUS_SUCCESS;
+}
+
+extern "C" gs_status gs_noalloc_device_error(void *stream, uint32_t *word) {
+    using namespace gs;
+    if (!word) return GS_STATUS_INVALID_VALUE;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return GS_STATUS_NOT_INITIALIZED;
+    }
+    DeviceSlot *slot = nullptr;
+    gs_status st = device_slot(dev, &slot);
+    if (st != GS_STATUS_SUCCESS) return st;
+    // The word sits right after the tensor maps; a plain device-to-host copy of 4 bytes, no allocation.
+    if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess ||
+        cudaMemcpy(word, static_cast<unsigned char *>(slot->scratch) + kMapBytes, sizeof(uint32_t),
+                   cudaMemcpyDeviceToHost) != cudaSuccess) {
         cudaGetLastError();
         return GS_STATUS_EXECUTION_FAILED;
     }

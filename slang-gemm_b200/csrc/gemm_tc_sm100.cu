@@ -114,6 +114,8 @@ struct TcArgs {
     simt::SimtArgs fb;           // pointer-array batches: the CUDA-core fallback's view of the problem
     Epilogue ep;
     uint32_t *err;
+    long long spin_limit;        // SM cycles after which a bounded wait gives up
+    int debug_skip_kb;           // test hook (>= 0): the producer skips this K block of its first tile, then stops
 };
 
 __device__ __forceinline__ void tile_coords(const TcArgs &a, long long t, int &b, int &mb, int &nb) {
@@ -162,7 +164,8 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;
     uint64_t *tempty = tfull + 2;
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(tempty + 2);
+    uint64_t *drain = tempty + 2;  // the MMA issuer's last commit on an error path
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -192,6 +195,7 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
             // One elected lane per epilogue warp (of both CTAs for CG 2).
             mbar_init(&tempty[i], CG * C_::EPI_WARPS);
         }
+        mbar_init(drain, 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0 && args.a_maps == nullptr) {
@@ -241,7 +245,10 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     tensormap_acquire(mbp);
                 }
                 for (int kb = 0; kb < args.k_blocks; ++kb) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, 1)) { ok = false; break; }
+                    // Test hook: leave this stage unfilled (no expect_tx, no copy) and issue nothing more, so
+                    // the MMA issuer's wait for it runs out with no load left in flight.
+                    if (kb == args.debug_skip_kb && t == tile0) { ok = false; break; }
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, 1, args.spin_limit)) { ok = false; break; }
                     uint8_t *dA = smA + stage * C_::A_STAGE;
                     uint8_t *dB = smB + stage * C_::B_STAGE;
                     const int k0 = kb * BK;
@@ -308,7 +315,7 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                 const int acc = (WIDE || chunked) ? 0 : (it & 1);
                 const uint32_t acc_phase = WIDE ? (it & 1) : ((it >> 1) & 1);
                 if (!chunked) {
-                    if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, 2)) break;
+                    if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, 2, args.spin_limit)) { ok = false; break; }
                     tc_fence_after();
                 }
                 const uint32_t d_tmem = tmem_base + acc * BN;
@@ -347,14 +354,14 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     int st = stage;
                     uint32_t ph = phase;
                     for (int j = 0; j < P; ++j) {
-                        if (!mbar_wait(&full[st], ph, args.err, 3)) { ok = false; break; }
+                        if (!mbar_wait(&full[st], ph, args.err, 3, args.spin_limit)) { ok = false; break; }
                         tc_fence_after();
                         issue(st, 0, j == 0);
                         if (j + 1 == args.k_blocks) commit_to(&tfull[0]);
                         if (++st == STAGES) { st = 0; ph ^= 1u; }
                     }
                     if (!ok) break;
-                    if (!mbar_wait(&tempty[1], acc_phase ^ 1u, args.err, 2)) break;
+                    if (!mbar_wait(&tempty[1], acc_phase ^ 1u, args.err, 2, args.spin_limit)) { ok = false; break; }
                     tc_fence_after();
                     for (int j = 0; j < P; ++j) {
                         issue(stage, 1, j == 0);
@@ -374,10 +381,10 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     const int kb_in = chunked ? kb % CHUNK_KB : kb;  // stage within the accumulator fill
                     if (chunked && kb_in == 0) {
                         // the epilogue has folded the previous fill into the running sum
-                        if (!mbar_wait(&tempty[0], (chunks & 1u) ^ 1u, args.err, 2)) { ok = false; break; }
+                        if (!mbar_wait(&tempty[0], (chunks & 1u) ^ 1u, args.err, 2, args.spin_limit)) { ok = false; break; }
                         tc_fence_after();
                     }
-                    if (!mbar_wait(&full[stage], phase, args.err, 3)) { ok = false; break; }
+                    if (!mbar_wait(&full[stage], phase, args.err, 3, args.spin_limit)) { ok = false; break; }
                     tc_fence_after();
 #pragma unroll
                     for (int s = 0; s < C_::NSUB; ++s) {
@@ -397,7 +404,7 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     int st = stage;
                     uint32_t ph = phase;
                     for (int j = 0; j < tail; ++j) {
-                        if (!mbar_wait(&full[st], ph, args.err, 3)) { ok = false; break; }
+                        if (!mbar_wait(&full[st], ph, args.err, 3, args.spin_limit)) { ok = false; break; }
                         tc_fence_after();
                         issue(st, 0, false);
                         if (++st == STAGES) { st = 0; ph ^= 1u; }
@@ -411,6 +418,12 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                     }
                 }
                 if (ok && !chunked) commit_to(&tfull[WIDE ? 1 : acc]);
+            }
+            if (!ok) {
+                // A wait gave up: before the CTA tears down (and frees TMEM), wait, again within the limit,
+                // until the MMAs already issued have completed.
+                commit_to(drain);
+                mbar_wait(drain, 0, args.err, 5, args.spin_limit);
             }
         }
     } else {
@@ -445,7 +458,11 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                 // Fold every fill but the last into the running sum (columns BN..2BN-1), in order.
 #pragma unroll 1
                 for (int f = 0; ok && f + 1 < nfills; ++f) {
-                    if (!mbar_wait(&tfull[0], echunks & 1u, args.err, 4)) { ok = false; break; }
+                    // every lane of the warp takes the same way out (tcgen05.ld below is warp-aligned)
+                    if (!__all_sync(0xffffffffu, mbar_wait(&tfull[0], echunks & 1u, args.err, 4, args.spin_limit))) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
 #pragma unroll 1
                     for (int c = c_lo; c < c_lo + C_::EPI_COLS; c += 32) {
@@ -479,7 +496,10 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
             for (int half = 0; half < C_::NSUB; ++half) {
             const int acc = WIDE ? half : (chunked ? 0 : (it & 1));
             const uint32_t acc_phase = chunked ? (echunks & 1u) : (WIDE ? (it & 1) : ((it >> 1) & 1));
-            if (!mbar_wait(&tfull[acc], acc_phase, args.err, 4)) { ok = false; break; }
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, args.err, 4, args.spin_limit))) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
             const int n0 = nb * TILE_N + half * BN;  // tile column of this slot's first accumulator column
             const int ncols = min(BN, args.n - n0);
@@ -777,6 +797,8 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int shape) {
     a.ab_evict_last = d.batch == 1 ? 1 : 0;
     a.ep = d.ep;
     a.err = ctx.dev_err;
+    a.spin_limit = ctx.spin_limit;
+    a.debug_skip_kb = ctx.debug_skip_kb;
     return a;
 }
 
@@ -867,12 +889,25 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     // swaps in each batch entry's address.
     const size_t need = 3 * static_cast<size_t>(d.batch) * sizeof(CUtensorMap);
     if (ctx.tmap_bytes < need) {
-        if (ctx.tmap_buf) cudaFree(ctx.tmap_buf);
-        ctx.tmap_buf = nullptr;
-        ctx.tmap_bytes = 0;
-        cudaError_t e = cudaMalloc(&ctx.tmap_buf, need);
+        // Grow-only, checked before anything of this call is enqueued. The old buffer may still be read
+        // by kernels in flight, so it is not freed here (cudaFree would synchronise the device): it is
+        // retired and freed with the handle. The first allocation holds 1024 entries and growth at least
+        // doubles, so the retired buffers together stay smaller than the live one.
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(ctx.stream, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone) {
+            ctx.last_error = "the pointer-array tensor-map buffer must grow, which cannot be captured: make one "
+                             "call with this batch count before the stream capture";
+            return cudaErrorStreamCaptureUnsupported;
+        }
+        size_t bytes = 3 * size_t(1024) * sizeof(CUtensorMap);
+        if (bytes < 2 * ctx.tmap_bytes) bytes = 2 * ctx.tmap_bytes;
+        if (bytes < need) bytes = need;
+        void *grown = nullptr;
+        cudaError_t e = cudaMalloc(&grown, bytes);
         if (e != cudaSuccess) return e;
-        ctx.tmap_bytes = need;
+        if (ctx.tmap_buf) ctx.retired.push_back(ctx.tmap_buf);
+        ctx.tmap_buf = grown;
+        ctx.tmap_bytes = bytes;
     }
     CUtensorMap ta, tb;
     std::string why;

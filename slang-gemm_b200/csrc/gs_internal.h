@@ -2,6 +2,7 @@
 #pragma once
 #include <cstdint>
 #include <string>
+#include <vector>
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -46,11 +47,17 @@ struct Plan {
 };
 
 // Host-side context behind gs_handle.
+// Default limit of the kernels' bounded waits: 4e9 SM cycles, about 2 s at the
+// B200's 1.965 GHz top clock; any legitimate wait in these kernels is far shorter.
+constexpr long long kDefaultWaitLimitCycles = 4000000000LL;
+
 struct Context {
     int device = -1;
     int sm_count = 0;
     cudaStream_t stream = nullptr;
     uint32_t *dev_err = nullptr;      // [0] error word of bounded waits, [1] / [2] pointer-array A,B / C misalignment flags
+    long long spin_limit = kDefaultWaitLimitCycles;  // SM cycles after which a bounded wait gives up
+    int debug_skip_kb = -1;           // test hook of gs_debug_skip_kblock (-1 = off)
     uint32_t last_kernels = 0;
     uint64_t launches = 0;
     std::string last_error;
@@ -62,9 +69,10 @@ struct Context {
     static constexpr int kMaxChunks = 32;
     cudaEvent_t ev_start = nullptr, ev_a = nullptr;
     cudaEvent_t ev_in[kMaxChunks] = {}, ev_out[kMaxChunks] = {};
-    // device copy of tensor maps for pointer-array batches
+    // device copy of tensor maps for pointer-array batches; buffers it outgrew are freed with the handle
     void *tmap_buf = nullptr;
     size_t tmap_bytes = 0;
+    std::vector<void *> retired;
     // split operands of the FAST_TF32 tensor-core path
     void *tf32_buf = nullptr;
     size_t tf32_bytes = 0;

@@ -1,10 +1,11 @@
 // gs_ptx.cuh -- thin inline-PTX wrappers for sm_100a: mbarriers, TMA tiled
 // loads, tcgen05 (TMEM allocation, UMMA issue/commit, TMEM loads).
 //
-// Every wait on an mbarrier is bounded: after kSpinLimitCycles of SM clock the
-// wait gives up, records GS_DEVERR_TIMEOUT plus a site code in the kernel's
-// error word and returns false, so a broken pipeline ends the kernel with an
-// error status instead of hanging the GPU.
+// Every wait on an mbarrier is bounded: after a limit of SM clock cycles (a
+// kernel argument: the handle's wait limit, about 2 s by default) the wait
+// gives up, records GS_DEVERR_TIMEOUT plus a site code in the kernel's error
+// word and returns false, so a broken pipeline ends the kernel with an error
+// status instead of hanging the GPU.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -14,8 +15,9 @@ namespace gs {
 // Device error word layout: bit 0 = a wait timed out; bits 8..15 = site code
 // of the first timeout.
 constexpr uint32_t GS_DEVERR_TIMEOUT = 1u;
-// About 4 s at 1 GHz; any legitimate wait in these kernels is far shorter.
-constexpr long long kSpinLimitCycles = 4000000000LL;
+// Suspend-time hint of one try_wait, in ns: a waiting thread sleeps until the
+// phase completes or this much time has passed, instead of re-polling.
+constexpr uint32_t kTryWaitHintNs = 1000000;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -55,15 +57,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
     return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity. Returns false (and sets
-// the error word) if the limit ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t site) {
+// try_wait with a suspend-time hint (ns).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar_addr, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t"
+        ".reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "}\n"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity: gives up after `limit` SM
+// clock cycles. Returns false (and sets the error word) if the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t site,
+                                          long long limit) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const long long start = clock64();
     while (true) {
-        if (mbar_try_wait(addr, parity)) return true;
-        if (clock64() - start > kSpinLimitCycles) {
+        if (mbar_try_wait_hint(addr, parity, kTryWaitHintNs)) return true;
+        if (clock64() - start > limit) {
             if (err) atomicCAS(err, 0u, GS_DEVERR_TIMEOUT | (site << 8));
             return false;
         }

@@ -118,6 +118,8 @@ def _load() -> ctypes.CDLL:
         "gs_last_kernels": (u32, [vp]),
         "gs_launch_count": (ctypes.c_uint64, [vp]),
         "gs_device_error": (st, [vp, ctypes.POINTER(u32)]),
+        "gs_set_wait_limit": (st, [vp, ll]),
+        "gs_debug_skip_kblock": (st, [vp, i]),
         "gs_sgemm": (st, [vp, i, i, i, i, i, vp, vp, i, vp, i, vp, vp, i]),
         "gs_sgemm_strided_batched": (st, [vp, i, i, i, i, i, vp, vp, i, ll, vp, i, ll, vp, vp, i, ll, i]),
         "gs_hgemm": (st, [vp, i, i, i, i, i, vp, vp, i, vp, i, vp, vp, i]),
@@ -131,6 +133,7 @@ def _load() -> ctypes.CDLL:
         "gs_host_gemm_batched_ex": (st, [vp, ctypes.POINTER(PtrBatchedDesc)]),
         "gs_plan_shards": (st, [ll, i, ll, ctypes.POINTER(ll)]),
         "gs_gemm_batched_ex_noalloc": (st, [vp, i, i, i, i, i, vp, vp, i, i, vp, i, i, vp, vp, i, i, i, i]),
+        "gs_noalloc_device_error": (st, [vp, ctypes.POINTER(u32)]),
         "gs_multi_create": (st, [ctypes.POINTER(vp), i, ctypes.POINTER(i)]),
         "gs_multi_destroy": (st, [vp]),
         "gs_multi_last_error": (ctypes.c_char_p, [vp]),
@@ -227,6 +230,14 @@ def gemm_batched_ex_noalloc(stream, transa, transb, m, n, k, alpha, Aarr, atype,
                                            compute)
 
 
+def noalloc_device_error(stream=None) -> tuple[int, int]:
+    """gs_noalloc_device_error: (status, word) -- the device error word of the last
+    gs_gemm_batched_ex_noalloc call on the current device, read after synchronising `stream`."""
+    w = ctypes.c_uint32(0)
+    s = _lib.gs_noalloc_device_error(getattr(stream, "cuda_stream", stream), ctypes.byref(w))
+    return s, w.value
+
+
 @dataclass
 class _Stream:
     ptr: int
@@ -280,6 +291,14 @@ class Handle:
         w = ctypes.c_uint32(0)
         self._check(_lib.gs_device_error(self._h, ctypes.byref(w)), "gs_device_error")
         return w.value
+
+    def set_wait_limit(self, cycles: int):
+        """gs_set_wait_limit: SM cycles after which the kernels' bounded waits give up (<= 0: the default)."""
+        self._check(_lib.gs_set_wait_limit(self._h, int(cycles)), "gs_set_wait_limit")
+
+    def debug_skip_kblock(self, kblock: int):
+        """gs_debug_skip_kblock: test hook that leaves one K block of the first tile unfilled (-1 = off)."""
+        self._check(_lib.gs_debug_skip_kblock(self._h, int(kblock)), "gs_debug_skip_kblock")
 
     def _check(self, s: int, what: str):
         if s != STATUS_SUCCESS:

@@ -4,13 +4,19 @@ gs_gemm_ex_colsplit_multi) over every visible GPU, and over one GPU.
 
 Each device computes its shard with the same kernel and the same K order as
 the single-GPU call, so its part of C must equal the single-GPU result bit for
-bit; the single-GPU result itself is pinned to the oracle by the parity tests.
-Gathered C (NCCL point to point) must equal it everywhere it was gathered.
+bit. Gathered C (NCCL point to point) must equal it everywhere it was gathered.
+Both the single-GPU result and every gathered C are also compared with the CPU
+oracle (the reference's gemmExCuda, src/gemm.zig:671-706) on the same bytes:
+bit-exact for INT8 -> INT32, normwise relative error within the FP16 / BF16
+bounds otherwise.
 """
+import numpy as np
 import pytest
 import torch
 
 import gemm_sm100 as gs
+import oracle as orc
+from gpu_util import assert_parity
 
 pytestmark = pytest.mark.gpu
 
@@ -33,13 +39,35 @@ def _inputs(dt, count, seed):
     return (torch.randn(count, generator=g) * 0.25).to(TORCH_OF[dt])
 
 
+def _np(t):
+    """Host bytes of a CPU tensor as the oracle reads them (16-bit floats as raw uint16 bits)."""
+    if t.dtype in (torch.float16, torch.bfloat16):
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+def _oracle(dt, ct, comp, ta, tb, m, n, k, batch, lda, ldb, ldc, sa, sb, sc, A, B, beta, C0) -> np.ndarray:
+    c = _np(C0).copy()
+    assert orc.gemm_ex(ta, tb, m, n, k, 1.0, _np(A), dt, lda, _np(B), dt, ldb, beta, c, ct, ldc, compute_type=comp,
+                       batch=batch, sa=sa, sb=sb, sc=sc, threads=8) == orc.OK
+    return c
+
+
+def _check_oracle(got, want, dt, ct):
+    assert_parity(_np(got), want, ct, dt if dt != gs.R_8I else gs.R_32F)
+
+
 def _ref_strided(dt, ct, comp, ta, tb, m, n, k, batch, lda, ldb, ldc, sa, sb, sc, A, B, beta, C0):
+    """(single-GPU result, oracle result); the first is checked against the second here."""
     h = gs.Handle()
     Ad, Bd, Cd = A.cuda(0), B.cuda(0), C0.clone().cuda(0)
     h.gemm_strided_batched_ex(ta, tb, m, n, k, 1, Ad, dt, lda, sa, Bd, dt, ldb, sb, beta, Cd, ct, ldc, sc, batch,
                               comp)
     torch.cuda.synchronize(0)
-    return Cd.cpu()
+    out = Cd.cpu()
+    want = _oracle(dt, ct, comp, ta, tb, m, n, k, batch, lda, ldb, ldc, sa, sb, sc, A, B, beta, C0)
+    _check_oracle(out, want, dt, ct)
+    return out, want
 
 
 @pytest.mark.parametrize("devs", device_sets(), ids=lambda d: f"gpus{len(d)}")
@@ -57,7 +85,7 @@ def test_strided_batched_multi(devs, dt, ta, tb, m, n, k, batch, beta, gather):
     A, B = _inputs(dt, sa * batch, 1), _inputs(dt, sb * batch, 2)
     C0 = (torch.randint(-50, 50, (sc * batch,), dtype=torch.int32) if ct == gs.R_32I
           else torch.randn(sc * batch, dtype=torch.float32))
-    ref = _ref_strided(dt, ct, comp, ta, tb, m, n, k, batch, lda, ldb, ldc, sa, sb, sc, A, B, beta, C0)
+    ref, want = _ref_strided(dt, ct, comp, ta, tb, m, n, k, batch, lda, ldb, ldc, sa, sb, sc, A, B, beta, C0)
 
     mh = gs.MultiHandle(devs)
     As = [A.cuda(d) for d in devs]
@@ -73,6 +101,7 @@ def test_strided_batched_multi(devs, dt, ta, tb, m, n, k, batch, beta, gather):
         assert torch.equal(got[lo:hi], ref[lo:hi]), f"device {d} shard differs"
         if gather == gs.GATHER_ALL or (gather == g) or len(devs) == 1:
             assert torch.equal(got, ref), f"device {d} gathered C differs"
+            _check_oracle(got, want, dt, ct)
         elif gather == gs.GATHER_NONE:
             rest = torch.ones(got.numel(), dtype=torch.bool)
             rest[lo:hi] = False
@@ -95,7 +124,7 @@ def test_colsplit_multi(devs, dt, ta, tb, m, n, k, gather):
     lda, ldb, ldc = (m if ta == 0 else k), (k if tb == 0 else n), m
     A, B = _inputs(dt, m * k, 3), _inputs(dt, k * n, 4)
     C0 = torch.zeros(m * n, dtype=TORCH_OF[ct])
-    ref = _ref_strided(dt, ct, comp, ta, tb, m, n, k, 1, lda, ldb, ldc, 0, 0, 0, A, B, 0.0, C0)
+    ref, want = _ref_strided(dt, ct, comp, ta, tb, m, n, k, 1, lda, ldb, ldc, 0, 0, 0, A, B, 0.0, C0)
     mh = gs.MultiHandle(devs)
     As = [A.cuda(d) for d in devs]
     Bs = [B.cuda(d) for d in devs]
@@ -108,6 +137,7 @@ def test_colsplit_multi(devs, dt, ta, tb, m, n, k, gather):
         assert torch.equal(got[lo:hi], ref[lo:hi]), f"device {d} column block differs"
         if gather == g or len(devs) == 1:
             assert torch.equal(got, ref)
+            _check_oracle(got, want, dt, ct)
     mh.close()
 
 
@@ -119,8 +149,8 @@ def test_pointer_array_multi(devs):
     mats_b = [_inputs(dt, k * n, 40 + i) for i in range(batch)]
     A = torch.cat(mats_a)
     B = torch.cat(mats_b)
-    ref = _ref_strided(dt, ct, comp, 0, 0, m, n, k, batch, m, k, m, m * k, k * n, m * n, A, B, 0.0,
-                       torch.zeros(m * n * batch))
+    ref, want = _ref_strided(dt, ct, comp, 0, 0, m, n, k, batch, m, k, m, m * k, k * n, m * n, A, B, 0.0,
+                             torch.zeros(m * n * batch))
     mh = gs.MultiHandle(devs)
     keep, arrs = [], ([], [], [])
     for d in devs:
@@ -139,6 +169,7 @@ def test_pointer_array_multi(devs):
             got = c_list[i].cpu()
             if off[g] <= i < off[g + 1]:
                 assert torch.equal(got, ref[i * m * n:(i + 1) * m * n]), f"device {d} entry {i}"
+                _check_oracle(got, want[i * m * n:(i + 1) * m * n], dt, ct)
             else:
                 assert not got.any(), f"device {d} wrote entry {i} outside its shard"
     mh.close()
