@@ -462,20 +462,23 @@ def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str
     value = total_flops / (ms_per_step * 1e-3) / 1e12
 
     # ---- end to end through the host-buffer entry point ----
-    Ah = A.cpu().pin_memory()
-    Bh = B.cpu().pin_memory()
-    Ch = C.cpu().pin_memory()
-    e2e_steps = max(1, min(args.steps, 20))
-    call_host(h, cfg, Ah, Bh, Ch)  # warm the staging buffers
-    barrier(dist)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        call_host(h, cfg, Ah, Bh, Ch)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1)) / e2e_steps
-    e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
+    e2e_ms = e2e_value = None
+    if not args.no_e2e:
+        Ah = A.cpu().pin_memory()
+        Bh = B.cpu().pin_memory()
+        Ch = C.cpu().pin_memory()
+        e2e_steps = max(1, min(args.steps, 20))
+        call_host(h, cfg, Ah, Bh, Ch)  # warm the staging buffers
+        barrier(dist)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            call_host(h, cfg, Ah, Bh, Ch)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1)) / e2e_steps
+        e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
+        del Ah, Bh, Ch
     h2d = A.numel() * A.element_size() + B.numel() * B.element_size()
     if cfg["beta"] != 0:
         h2d += C.numel() * C.element_size()
@@ -499,7 +502,8 @@ def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str
         "config": config_dict(cfg0, cfg, world, scaling, 0 if world > 1 else args.shard_of),
         "e2e": {"value": round(e2e_value, 2), "unit": unit, "h2d_bytes_per_step": h2d * world,
                 "d2h_bytes_per_step": d2h * world, "ms_per_step": round(e2e_ms, 3),
-                "path": "gs_host_gemm_ex (pinned host buffers; H2D, kernel, D2H, stream sync per step)"},
+                "path": "gs_host_gemm_ex (pinned host buffers; H2D, kernel, D2H, stream sync per step)"}
+        if e2e_value is not None else {"skipped": "--no-e2e (a profiling run)"},
         "roofline": roof,
         "pipe_utilization": committed_pipe_utilization(cfg_name),
         "gpu_launches": int(launches),
@@ -944,6 +948,7 @@ def main():
     ap.add_argument("--cublas", dest="cublas", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--gather", action="store_true", help="N > 1: also time an NCCL all-gather of C (separately)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs only)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the cpu_baseline sample")
     ap.add_argument("--ref-seconds", type=float, default=90.0, help="target total length of --impl reference")
     ap.add_argument("--algo", type=int, default=-1,
