@@ -187,6 +187,8 @@ gs_status gs_destroy(gs_handle h) {
     if (h->ctx.dev_err) cudaFree(h->ctx.dev_err);
     if (h->ctx.stage) cudaFree(h->ctx.stage);
     if (h->ctx.tmap_buf) cudaFree(h->ctx.tmap_buf);
+    if (h->ctx.sk_buf) cudaFree(h->ctx.sk_buf);
+    if (h->ctx.sk_counts) cudaFree(h->ctx.sk_counts);
     for (void *p : h->ctx.retired) cudaFree(p);
     if (h->ctx.tf32_buf) cudaFree(h->ctx.tf32_buf);
     if (h->ctx.h2d) cudaStreamDestroy(h->ctx.h2d);

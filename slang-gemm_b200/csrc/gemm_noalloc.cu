@@ -111,6 +111,7 @@ extern "C" gs_status gs_gemm_batched_ex_noalloc(void *stream, int transa, int tr
     ctx.device = dev;
     ctx.sm_count = slot->sm_count;
     ctx.stream = static_cast<cudaStream_t>(stream);
+    ctx.may_allocate = false;
     ctx.tmap_buf = slot->scratch;
     ctx.tmap_bytes = kMapBytes;
     ctx.dev_err = reinterpret_cast<uint32_t *>(static_cast<unsigned char *>(slot->scratch) + kMapBytes);

@@ -826,9 +826,9 @@ static double slot_use(const GemmDesc &d, int tile_n, long long pairs, long long
 // batch-4 4096x4096x1024 FP16 0.122 -> 0.118 ms, batch-9/11/13
 // 2048x2048x1536 0.095/0.116/0.135 -> 0.093/0.113/0.134); where it fills its
 // last round worse (batch-8 2048x2048x1536 FP16 0.085 -> 0.093) the pair tile
-// stays. INT8 keeps the pair tile there: batch-9/11/13 2048^3 ran 3-4 %
-// slower on the wide tile, and batch-64 2048^3 (C5b) measured between 4 %
-// faster and even across boxes.
+// stays. INT8 takes the wide tile there only for long persistent runs (at
+// least 16 rounds of wide tiles): batch-9/11/13 2048^3 (4-6 rounds) ran 3-4 %
+// slower on it, batch-64 2048^3 (C5b, 28 rounds) 1-4 % faster on three boxes.
 static int choose_shape_any(const GemmDesc &d, long long pairs);
 static int choose_shape(const Context &ctx, const GemmDesc &d) {
     const int shape = choose_shape_any(d, ctx.sm_count >= 2 ? ctx.sm_count / 2 : 1);
@@ -852,9 +852,10 @@ static int choose_shape_any(const GemmDesc &d, long long pairs) {
                                                         (d.ep.beta_zero ? 1.0 : 2.0);
     const double ridge = d.in_kind == IN_I8 ? 520.0 : 260.0;
     if (flops / bytes < ridge) return 3;
-    if (d.in_kind != IN_F16 && d.in_kind != IN_BF16) return 2;
     long long rounds_wide = 0, rounds_pair = 0;
     const double use_wide = slot_use(d, 2 * BN, pairs, &rounds_wide);
+    if (d.in_kind == IN_I8) return rounds_wide >= 16 ? 3 : 2;
+    if (d.in_kind != IN_F16 && d.in_kind != IN_BF16) return 2;
     const double use_pair = slot_use(d, BN, pairs, &rounds_pair);
     return rounds_wide >= 4 && use_wide >= use_pair - 1e-3 ? 3 : 2;
 }

@@ -73,6 +73,13 @@ struct Context {
     void *tmap_buf = nullptr;
     size_t tmap_bytes = 0;
     std::vector<void *> retired;
+    // stream-K workspace of the FP32 FFMA kernel: two partial tiles per resident CTA, and per-tile counters
+    void *sk_buf = nullptr;
+    size_t sk_bytes = 0;
+    void *sk_counts = nullptr;
+    size_t sk_count_bytes = 0;
+    // false for contexts over caller-provided memory only (the no-allocation entry point)
+    bool may_allocate = true;
     // split operands of the FAST_TF32 tensor-core path
     void *tf32_buf = nullptr;
     size_t tf32_bytes = 0;

@@ -171,6 +171,129 @@ __device__ __forceinline__ void store4(float *p, float4 v, const Epilogue &ep) {
     *reinterpret_cast<float4 *>(p) = v;
 }
 
+// Row lengths of the shared-memory operand tiles (As[k][m], Bs[k][n], double buffered); rows are padded
+// when they are filled by transposing stores.
+template <int TA, int TB, class T>
+struct Smem {
+    static constexpr int LDA_S = T::BM + (TA == 1 ? 4 : 0);
+    static constexpr int LDB_S = T::BN + (TB == 0 ? 4 : 0);
+};
+
+// Accumulates op(A)[m0.., k] x op(B)[k, n0..] over the K steps [kt0, kt1) of one tile into acc2
+// (acc2[ip][j] = rows 2ip, 2ip+1 of this thread, column j). Starts and ends with the CTA synchronised, so
+// the shared tiles are free again when it returns. Used by the stream-K kernel; the data-parallel kernel
+// below keeps the same loop written inline, where ptxas allocates it fewer registers (4-12 bytes of spill
+// for the 128 x 128 tile instead of 60-104 through this function, -Xptxas -v).
+template <int TA, int TB, class T>
+__device__ __forceinline__ void k_loop(const FfmaArgs &a, const float *A, const float *B, int m0, int n0, int kt0,
+                                       int kt1, bool va, bool vb,
+                                       float (&As)[2][T::BK * Smem<TA, TB, T>::LDA_S],
+                                       float (&Bs)[2][T::BK * Smem<TA, TB, T>::LDB_S],
+                                       float2 (&acc2)[2 * T::RM][4 * T::RN]) {
+    constexpr int BM = T::BM, BN = T::BN, BK = T::BK, RM = T::RM, RN = T::RN;
+    constexpr int LDA_S = Smem<TA, TB, T>::LDA_S, LDB_S = Smem<TA, TB, T>::LDB_S;
+    const int tid = threadIdx.x;
+    const int tx = tid % T::TX, ty = tid / T::TX;
+    const bool full_m = m0 + BM <= a.m, full_n = n0 + BN <= a.n;
+    float4 ra[T::CH_A], rb[T::CH_B];
+    if (kt0 < kt1) {
+        const int k0 = kt0 * BK;
+        const bool fk = k0 + BK <= a.k;
+#pragma unroll
+        for (int i = 0; i < T::CH_A; ++i) load_a<TA, T>(a, A, m0, k0, tid + i * T::THREADS, va && full_m && fk, ra[i]);
+#pragma unroll
+        for (int i = 0; i < T::CH_B; ++i) load_b<TB, T>(a, B, n0, k0, tid + i * T::THREADS, vb && full_n && fk, rb[i]);
+#pragma unroll
+        for (int i = 0; i < T::CH_A; ++i) store_a<TA, T>(As[0], LDA_S, tid + i * T::THREADS, ra[i]);
+#pragma unroll
+        for (int i = 0; i < T::CH_B; ++i) store_b<TB, T>(Bs[0], LDB_S, tid + i * T::THREADS, rb[i]);
+    }
+    __syncthreads();
+
+    for (int kt = kt0; kt < kt1; ++kt) {
+        const int cur = (kt - kt0) & 1;
+        const bool more = kt + 1 < kt1;
+        if (more) {
+            const int k0 = (kt + 1) * BK;
+            const bool fk = k0 + BK <= a.k;
+#pragma unroll
+            for (int i = 0; i < T::CH_A; ++i)
+                load_a<TA, T>(a, A, m0, k0, tid + i * T::THREADS, va && full_m && fk, ra[i]);
+#pragma unroll
+            for (int i = 0; i < T::CH_B; ++i)
+                load_b<TB, T>(a, B, n0, k0, tid + i * T::THREADS, vb && full_n && fk, rb[i]);
+        }
+        const float *as = As[cur];
+        const float *bs = Bs[cur];
+        float4 fa[2][RM], fb[2][RN];
+#pragma unroll
+        for (int r = 0; r < RM; ++r) fa[0][r] = *reinterpret_cast<const float4 *>(&as[r * (BM / RM) + tx * 4]);
+#pragma unroll
+        for (int r = 0; r < RN; ++r) fb[0][r] = *reinterpret_cast<const float4 *>(&bs[r * (BN / RN) + ty * 4]);
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            const int f = kk & 1;
+            if (kk + 1 < BK) {
+#pragma unroll
+                for (int r = 0; r < RM; ++r)
+                    fa[f ^ 1][r] = *reinterpret_cast<const float4 *>(&as[(kk + 1) * LDA_S + r * (BM / RM) + tx * 4]);
+#pragma unroll
+                for (int r = 0; r < RN; ++r)
+                    fb[f ^ 1][r] = *reinterpret_cast<const float4 *>(&bs[(kk + 1) * LDB_S + r * (BN / RN) + ty * 4]);
+            }
+            // Packed FP32 FMA (FFMA2): two rows of one output column per instruction, each
+            // element rounded once exactly as fmaf rounds it.
+#pragma unroll
+            for (int j = 0; j < 4 * RN; ++j) {
+                const float4 &vbv = fb[f][j / 4];
+                const float bv = (j & 3) == 0 ? vbv.x : (j & 3) == 1 ? vbv.y : (j & 3) == 2 ? vbv.z : vbv.w;
+                const float2 b2 = make_float2(bv, bv);
+#pragma unroll
+                for (int ip = 0; ip < 2 * RM; ++ip) {
+                    const float4 &vav = fa[f][ip / 2];
+                    const float2 a2 = (ip & 1) ? make_float2(vav.z, vav.w) : make_float2(vav.x, vav.y);
+                    acc2[ip][j] = __ffma2_rn(a2, b2, acc2[ip][j]);
+                }
+            }
+        }
+        if (more) {
+#pragma unroll
+            for (int i = 0; i < T::CH_A; ++i) store_a<TA, T>(As[cur ^ 1], LDA_S, tid + i * T::THREADS, ra[i]);
+#pragma unroll
+            for (int i = 0; i < T::CH_B; ++i) store_b<TB, T>(Bs[cur ^ 1], LDB_S, tid + i * T::THREADS, rb[i]);
+        }
+        __syncthreads();
+    }
+}
+
+// Writes a finished tile: rows m0 + r*(BM/RM) + tx*4 + {0..3}, columns n0 + s*(BN/RN) + ty*4 + {0..3};
+// alpha*acc then + beta*C with separate roundings, as gemm(f32) does (src/gemm.zig:523-544).
+template <class T>
+__device__ __forceinline__ void store_tile(const FfmaArgs &a, float *C, int m0, int n0, bool vc,
+                                           const float2 (&acc2)[2 * T::RM][4 * T::RN]) {
+    constexpr int BM = T::BM, BN = T::BN, RM = T::RM, RN = T::RN;
+    const int tx = threadIdx.x % T::TX, ty = threadIdx.x / T::TX;
+    const bool fast_c = vc && m0 + BM <= a.m && n0 + BN <= a.n;
+#pragma unroll
+    for (int j = 0; j < 4 * RN; ++j) {
+        const int gn = n0 + (j / 4) * (BN / RN) + ty * 4 + (j & 3);
+#pragma unroll
+        for (int r = 0; r < RM; ++r) {
+            const int gm = m0 + r * (BM / RM) + tx * 4;
+            const float v0 = acc2[2 * r][j].x, v1 = acc2[2 * r][j].y, v2 = acc2[2 * r + 1][j].x,
+                        v3 = acc2[2 * r + 1][j].y;
+            if (fast_c) {
+                store4(C + static_cast<size_t>(gn) * a.ldc + gm, make_float4(v0, v1, v2, v3), a.ep);
+            } else if (gn < a.n) {
+                const float vv[4] = {v0, v1, v2, v3};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (gm + i < a.m) store_facc<OUT_F32>(C, static_cast<size_t>(gn) * a.ldc + gm + i, vv[i], a.ep);
+            }
+        }
+    }
+}
+
 // S = 1: one CTA per tile, grid.x = M tiles. S > 1: clusters of S CTAs along x
 // share a tile (grid.x = M tiles * S), CTA rank r runs K steps [r*ceil(kt/S), ...).
 template <int TA, int TB, class T, int S>
@@ -347,6 +470,122 @@ __global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma(const FfmaAr
     }
 }
 
+// ---- stream-K: the (tile, K step) iterations of a launch spread evenly over the CTAs -------------------
+//
+// A launch of TileL tiles leaves SMs idle when its tile count is not a multiple of the 2 x 148 resident
+// CTAs (C2's 4096 x 1024 has 256 tiles: 40 SMs hold one CTA, 108 hold two, 13.5 % of the slots empty). The
+// stream-K kernel launches exactly the resident CTAs and gives CTA c the iterations [c*T/G, (c+1)*T/G)
+// of the T = tiles x K-steps iterations, tile by tile in order. A tile covered by one CTA is stored
+// directly. A tile split between CTAs is finished by the last of them to arrive: every contributor writes
+// its partial tile to its own workspace slot (one for the first tile of its range, one for the last), then
+// adds its K-step count to the tile's counter; the CTA whose addition completes the count sums all
+// contributors' slots in K order (the same order whoever arrives last, so results are deterministic),
+// applies alpha / beta, stores the tile and resets the counter for the next launch. No CTA waits for
+// another, so nothing depends on the CTAs being co-resident.
+
+struct SkArgs {
+    long long tiles;      // m tiles x n tiles x batch
+    int mt, nt;           // tile counts along M and N
+    int kt;               // K steps per tile
+    float4 *partials;     // 2 slots of BM x BN floats per CTA
+    unsigned *counts;     // per tile: K steps accumulated by partial contributors so far (0 between launches)
+};
+
+__device__ __forceinline__ long long sk_begin(long long c, long long total, long long g) { return c * total / g; }
+
+// The CTA whose iteration range holds iteration i.
+__device__ __forceinline__ long long sk_owner(long long i, long long total, long long g) {
+    long long c = i * g / total;
+    while (c + 1 < g && sk_begin(c + 1, total, g) <= i) ++c;
+    while (c > 0 && sk_begin(c, total, g) > i) --c;
+    return c;
+}
+
+template <int TA, int TB, class T>
+__global__ void __launch_bounds__(T::THREADS, T::MINB) k_sgemm_ffma_sk(const FfmaArgs a, const SkArgs s) {
+    constexpr int BM = T::BM, BN = T::BN, RM = T::RM, RN = T::RN;
+    constexpr int Q = BM * BN / 4 / T::THREADS;  // float4 of a partial tile per thread
+    static_assert(Q * 4 == 2 * RM * 4 * RN * 2, "partial tile / accumulator mismatch");
+    __shared__ __align__(16) float As[2][T::BK * Smem<TA, TB, T>::LDA_S];
+    __shared__ __align__(16) float Bs[2][T::BK * Smem<TA, TB, T>::LDB_S];
+    __shared__ int is_last;
+    grid_dep_wait();
+    grid_dep_launch();
+    const int tid = threadIdx.x;
+    const long long g = gridDim.x, c = blockIdx.x;
+    const long long total = s.tiles * s.kt;
+    const long long beg = sk_begin(c, total, g), end = sk_begin(c + 1, total, g);
+    const long long first_tile = beg / s.kt;
+    for (long long it = beg; it < end;) {
+        const long long tile = it / s.kt;
+        const int kb = static_cast<int>(it - tile * s.kt);
+        const int ke = static_cast<int>(end - tile * s.kt < s.kt ? end - tile * s.kt : s.kt);
+        const long long per_batch = static_cast<long long>(s.mt) * s.nt;
+        const int b = static_cast<int>(tile / per_batch);
+        const int r = static_cast<int>(tile - b * per_batch);
+        const int m0 = (r % s.mt) * BM, n0 = (r / s.mt) * BN;
+        const float *A = a.A + static_cast<size_t>(b) * a.stride_a;
+        const float *B = a.B + static_cast<size_t>(b) * a.stride_b;
+        float *C = a.C + static_cast<size_t>(b) * a.stride_c;
+        const bool va = a.vec_a && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
+        const bool vb = a.vec_b && (reinterpret_cast<uintptr_t>(B) & 15u) == 0;
+        const bool vc = a.vec_c && (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
+
+        float2 acc2[2 * RM][4 * RN];
+#pragma unroll
+        for (int i = 0; i < 2 * RM; ++i)
+#pragma unroll
+            for (int j = 0; j < 4 * RN; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
+        k_loop<TA, TB, T>(a, A, B, m0, n0, kb, ke, va, vb, As, Bs, acc2);
+
+        if (kb == 0 && ke == s.kt) {
+            store_tile<T>(a, C, m0, n0, vc, acc2);
+        } else {
+            // Partial tile: this CTA's slot for it, float4 q of thread tid at q * THREADS + tid.
+            float4 *slot = s.partials + (2 * c + (tile == first_tile ? 0 : 1)) * (BM * BN / 4);
+#pragma unroll
+            for (int q = 0; q < Q; ++q) {
+                const int ip = (2 * q) / (4 * RN), j = (2 * q) % (4 * RN);
+                slot[q * T::THREADS + tid] = make_float4(acc2[ip][j].x, acc2[ip][j].y, acc2[ip][j + 1].x,
+                                                         acc2[ip][j + 1].y);
+            }
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) {
+                const unsigned add = static_cast<unsigned>(ke - kb);
+                is_last = atomicAdd(&s.counts[tile], add) + add == static_cast<unsigned>(s.kt);
+            }
+            __syncthreads();
+            if (is_last) {
+                __threadfence();
+                // Sum the contributors' slots in K order (the CTAs whose ranges meet this tile).
+                const long long t0 = tile * s.kt;
+                const long long c_lo = sk_owner(t0, total, g), c_hi = sk_owner(t0 + s.kt - 1, total, g);
+#pragma unroll
+                for (int i = 0; i < 2 * RM; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4 * RN; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
+                for (long long cc = c_lo; cc <= c_hi; ++cc) {
+                    const long long cc_first = sk_begin(cc, total, g) / s.kt;
+                    const float4 *src = s.partials + (2 * cc + (tile == cc_first ? 0 : 1)) * (BM * BN / 4);
+#pragma unroll
+                    for (int q = 0; q < Q; ++q) {
+                        const int ip = (2 * q) / (4 * RN), j = (2 * q) % (4 * RN);
+                        const float4 v = __ldcg(src + q * T::THREADS + tid);
+                        acc2[ip][j].x += v.x;
+                        acc2[ip][j].y += v.y;
+                        acc2[ip][j + 1].x += v.z;
+                        acc2[ip][j + 1].y += v.w;
+                    }
+                }
+                store_tile<T>(a, C, m0, n0, vc, acc2);
+                if (tid == 0) s.counts[tile] = 0;  // ready for the next launch
+            }
+        }
+        it = tile * s.kt + ke;
+    }
+}
+
 template <int TA, int TB, class T, int S>
 static cudaError_t go(Context &ctx, const FfmaArgs &a) {
     dim3 grid((a.m + T::BM - 1) / T::BM * S, (a.n + T::BN - 1) / T::BN, a.batch < 65535 ? a.batch : 65535);
@@ -366,6 +605,64 @@ static cudaError_t go_ops(Context &ctx, const GemmDesc &d, const FfmaArgs &a) {
 template <class T>
 static long long ctas(const GemmDesc &d) {
     return static_cast<long long>((d.m + T::BM - 1) / T::BM) * ((d.n + T::BN - 1) / T::BN) * d.batch;
+}
+
+// Stream-K launch over exactly the resident CTAs of tile T. The workspace (two partial tiles per CTA) and
+// the per-tile counters are handle-owned, separate and grow-only; counters are zeroed when allocated and
+// reset by the kernel after use, so every launch finds them at zero.
+template <int TA, int TB, class T>
+static cudaError_t go_sk(Context &ctx, const FfmaArgs &a, long long ctas_resident) {
+    SkArgs s{};
+    s.mt = (a.m + T::BM - 1) / T::BM;
+    s.nt = (a.n + T::BN - 1) / T::BN;
+    s.tiles = static_cast<long long>(s.mt) * s.nt * a.batch;
+    s.kt = (a.k + T::BK - 1) / T::BK;
+    const long long grid = ctas_resident;
+    const size_t part_bytes = static_cast<size_t>(grid) * 2 * T::BM * T::BN * sizeof(float);
+    const size_t count_bytes = static_cast<size_t>(s.tiles) * sizeof(unsigned);
+    if (ctx.sk_bytes < part_bytes || ctx.sk_count_bytes < count_bytes) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(ctx.stream, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone) {
+            ctx.last_error = "the FP32 stream-K workspace must grow, which cannot be captured: make one call of "
+                             "this size before the stream capture";
+            return cudaErrorStreamCaptureUnsupported;
+        }
+    }
+    if (ctx.sk_bytes < part_bytes) {
+        const size_t bytes = part_bytes > 2 * ctx.sk_bytes ? part_bytes : 2 * ctx.sk_bytes;
+        void *grown = nullptr;
+        const cudaError_t e = cudaMalloc(&grown, bytes);
+        if (e != cudaSuccess) return e;
+        if (ctx.sk_buf) ctx.retired.push_back(ctx.sk_buf);  // kernels in flight may still read it
+        ctx.sk_buf = grown;
+        ctx.sk_bytes = bytes;
+    }
+    if (ctx.sk_count_bytes < count_bytes) {
+        const size_t bytes = count_bytes > 2 * ctx.sk_count_bytes ? count_bytes : 2 * ctx.sk_count_bytes;
+        void *grown = nullptr;
+        cudaError_t e = cudaMalloc(&grown, bytes);
+        if (e != cudaSuccess) return e;
+        e = cudaMemsetAsync(grown, 0, bytes, ctx.stream);  // counters start at zero; kernels leave them zero
+        if (e != cudaSuccess) {
+            cudaFree(grown);
+            return e;
+        }
+        if (ctx.sk_counts) ctx.retired.push_back(ctx.sk_counts);
+        ctx.sk_counts = grown;
+        ctx.sk_count_bytes = bytes;
+    }
+    s.partials = static_cast<float4 *>(ctx.sk_buf);
+    s.counts = static_cast<unsigned *>(ctx.sk_counts);
+    const cudaError_t e = launch_pdl(k_sgemm_ffma_sk<TA, TB, T>, dim3(static_cast<unsigned>(grid)), dim3(T::THREADS),
+                                     0, ctx.stream, 1, a, s);
+    ctx.launches++;
+    return e;
+}
+
+// Share of the resident CTA slots a data-parallel launch of `tiles` tiles keeps busy over its waves.
+static double wave_use(long long tiles, long long slots) {
+    const long long waves = (tiles + slots - 1) / slots;
+    return static_cast<double>(tiles) / static_cast<double>(waves * slots);
 }
 
 }  // namespace ffma
@@ -416,7 +713,21 @@ cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *
     // op(A) = T with op(B) = N is the one 128 x 128 variant that spills at 128
     // registers; the 64 x 64 tile is faster for it whenever its grid fills the GPU.
     const bool tn = d.trans_a && !d.trans_b;
-    if (ctas<TileL>(d) >= sms && !(tn && cm >= sms)) return go_ops<TileL>(ctx, d, a);
+    // Stream-K for a single partial wave of 128 x 128 tiles (at least one per SM, fewer than two full
+    // waves, more than a tenth of the resident slots idle) whose tiles have at least 64 K steps to amortise
+    // the partial-tile exchange: C2's 4096 x 1024 x 2048 (256 tiles on 296 slots) and 2048^3 measured 5-6 %
+    // faster. Measured slower and kept data-parallel: 32 K steps (1024 x 4096 x 512, 9 %), several waves
+    // (4096^3, 6 % even with the leading waves run data-parallel), and op T/N on the 64 x 64 tile (4-5 %).
+    // Handle calls only: it needs a workspace; pointer-array batches keep the per-entry grid.
+    const long long ctas_l = ctas<TileL>(d), slots = 2 * sms;
+    const int kt_l = (d.k + TileL::BK - 1) / TileL::BK;
+    if (ctx.may_allocate && a_arr == nullptr && !tn && ctas_l >= sms && ctas_l < 2 * slots && kt_l >= 64 &&
+        wave_use(ctas_l, slots) < 0.9) {
+        if (!d.trans_a && !d.trans_b) return go_sk<0, 0, TileL>(ctx, a, slots);
+        if (!d.trans_a && d.trans_b) return go_sk<0, 1, TileL>(ctx, a, slots);
+        return go_sk<1, 1, TileL>(ctx, a, slots);
+    }
+    if (ctas_l >= sms && !(tn && cm >= sms)) return go_ops<TileL>(ctx, d, a);
     if (cm >= sms) return go_ops<TileM>(ctx, d, a);
     const int ksteps = (d.k + TileM::BK - 1) / TileM::BK;
     int split = 1;

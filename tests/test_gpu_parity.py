@@ -457,3 +457,22 @@ def test_sgemm_cluster_split_k(handle, m, n, k, batch, pad, op_a, op_b):
     applied once, and bytes outside C unchanged."""
     run_case(handle, gs.R_32F, op_a, op_b, m, n, k, alpha=1.5, beta=-0.5, pad=pad, batch=batch, seed=m * n + k,
              expect_kernel=gs.KERNEL_FFMA)
+
+
+@pytest.mark.parametrize("m,n,k,batch,pad", [
+    (2100, 1300, 1100, 1, (0, 0, 0)),   # 187 tiles of 128 x 128 on 296 slots: ragged M, N and K, 69 K steps
+    (1500, 1100, 1030, 2, (0, 0, 0)),   # batched: 216 tiles, 65 K steps
+    (2048, 1536, 1040, 1, (1, 3, 2)),   # leading dimensions not multiples of 4: scalar loads and stores
+    (4096, 1024, 2048, 1, (0, 0, 0)),   # C2's shape: 256 tiles, each split over two CTAs
+])
+@pytest.mark.parametrize("op_a,op_b", [(0, 0), (0, 1), (1, 1), (1, 0)])
+def test_sgemm_stream_k(handle, m, n, k, batch, pad, op_a, op_b):
+    """FP32 problems whose 128 x 128 tiles fill less than two waves of the resident CTA slots, leaving some
+    idle, run stream-K (op T/N stays data-parallel): every CTA takes an equal share of the (tile, K step)
+    iterations and the last contributor to a split tile sums the partial tiles in K order. The result must
+    match the oracle to the FP32 tolerance, twice in a row on the same handle (the per-tile counters reset
+    themselves), with alpha and beta applied once and bytes outside C unchanged."""
+    for rep in range(2):
+        run_case(handle, gs.R_32F, op_a, op_b, m, n, k, alpha=1.5, beta=-0.5, pad=pad, batch=batch,
+                 seed=m + n + k + rep, expect_kernel=gs.KERNEL_FFMA)
+
