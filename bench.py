@@ -224,10 +224,10 @@ class ClockSampler:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
         s = sorted(self.samples)
-        b = sorted(self.busy)
+        b = self.busy
         names = [v for bit, v in self.REASONS.items() if self.reasons & bit and bit != 0x1]
         return {"sm_mhz": s[len(s) // 2], "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(s),
-                "gpu_busy_pct": b[len(b) // 2] if b else None}
+                "nvml_util_max_pct": max(b) if b else None}
 
 
 # ---- distributed plumbing -----------------------------------------------------
@@ -428,6 +428,7 @@ def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str
     launches0 = h.launch_count()
     sampler.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host_t0 = time.perf_counter()
     if flush is None:
         ev0.record(stream)
         for _ in range(args.steps):
@@ -449,11 +450,15 @@ def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str
         torch.cuda.synchronize()
         kernel_ms = sum(s0.elapsed_time(s1) for s0, s1 in evs) / max(1, args.steps)
         elapsed = kernel_ms * args.steps
+    host_ms = (time.perf_counter() - host_t0) * 1e3
+    # share of the timed region's host wall time (launches through the final synchronize) that this rank's
+    # GPU spent in the timed kernels
+    busy = min(1.0, elapsed / host_ms) if host_ms > 0 else 0.0
     clocks = sampler.stop()
     launches = h.launch_count() - launches0
     dev_err = h.device_error()
     barrier(dist)
-    per_rank = all_ranks(dist, [kernel_ms, clocks.get("gpu_busy_pct") or -1.0, clocks.get("sm_mhz") or -1.0])
+    per_rank = all_ranks(dist, [kernel_ms, busy, clocks.get("sm_mhz") or -1.0])
     max_elapsed = max_over_ranks(dist, elapsed)
     max_kernel_ms = max_over_ranks(dist, kernel_ms)
     flops_rank, bytes_rank = work(cfg)
@@ -507,6 +512,7 @@ def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str
         "roofline": roof,
         "pipe_utilization": committed_pipe_utilization(cfg_name),
         "gpu_launches": int(launches),
+        "device_busy": round(busy, 4),
         "clocks": clocks,
         "device_error_word": dev_err,
         "kernels": h.last_kernels(),
@@ -515,7 +521,7 @@ def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str
         import torch.distributed as tdist
 
         line["ranks"] = {"kernel_ms": [round(r[0], 4) for r in per_rank],
-                         "gpu_busy_pct": [r[1] if r[1] >= 0 else None for r in per_rank],
+                         "device_busy": [round(r[1], 4) for r in per_rank],
                          "sm_mhz": [r[2] if r[2] >= 0 else None for r in per_rank],
                          "units": [shard.cuts[g + 1] - shard.cuts[g] for g in range(world)],
                          "unit": "columns" if cfg0["shard"] == "cols" else "batch entries"}
