@@ -98,7 +98,10 @@ static gs_status fail(gs_handle h, gs_status st, const std::string &msg) {
 
 static gs_status from_cuda(gs_handle h, cudaError_t e, const char *where) {
     if (e == cudaSuccess) return GS_STATUS_SUCCESS;
-    return fail(h, GS_STATUS_EXECUTION_FAILED, std::string(where) + ": " + cudaGetErrorString(e));
+    std::string msg = std::string(where) + ": " + cudaGetErrorString(e);
+    // a launcher that refused to grow a buffer under stream capture said why
+    if (e == cudaErrorStreamCaptureUnsupported && h && !h->ctx.last_error.empty()) msg += " (" + h->ctx.last_error + ")";
+    return fail(h, GS_STATUS_EXECUTION_FAILED, msg);
 }
 
 extern "C" {
@@ -353,6 +356,7 @@ gs_status check_shape(gs_handle h, int transa, int transb, int m, int n, int k, 
 gs_status run(gs_handle h, GemmDesc &d) {
     Context &ctx = h->ctx;
     ctx.last_kernels = 0;
+    ctx.last_error.clear();
     Plan plan;
     std::string why;
     gs_status st = plan_gemm(d, &plan, &why);

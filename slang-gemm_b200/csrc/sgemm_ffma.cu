@@ -723,9 +723,11 @@ cudaError_t launch_ffma_ptr(Context &ctx, const GemmDesc &d, const void *const *
     const int kt_l = (d.k + TileL::BK - 1) / TileL::BK;
     if (ctx.may_allocate && a_arr == nullptr && !tn && ctas_l >= sms && ctas_l < 2 * slots && kt_l >= 64 &&
         wave_use(ctas_l, slots) < 0.9) {
-        if (!d.trans_a && !d.trans_b) return go_sk<0, 0, TileL>(ctx, a, slots);
-        if (!d.trans_a && d.trans_b) return go_sk<0, 1, TileL>(ctx, a, slots);
-        return go_sk<1, 1, TileL>(ctx, a, slots);
+        const cudaError_t e = !d.trans_a && !d.trans_b ? go_sk<0, 0, TileL>(ctx, a, slots)
+                              : !d.trans_a            ? go_sk<0, 1, TileL>(ctx, a, slots)
+                                                      : go_sk<1, 1, TileL>(ctx, a, slots);
+        if (e != cudaErrorMemoryAllocation) return e;
+        cudaGetLastError();  // no room for the workspace: the data-parallel grid below needs none
     }
     if (ctas_l >= sms && !(tn && cm >= sms)) return go_ops<TileL>(ctx, d, a);
     if (cm >= sms) return go_ops<TileM>(ctx, d, a);
