@@ -2,7 +2,8 @@
 sets kernel attributes and allocates the handle's tensor-map buffer), a call
 captured into a graph and replayed must give the same bits as the direct
 call, for every kernel family (tensor-core single / strided / pointer-array,
-FFMA, the FAST_TF32 split + tf32 GEMM, CUDA-core fallback, k = 0)."""
+FFMA data-parallel and stream-K, the FAST_TF32 split + tf32 GEMM, CUDA-core
+fallback, k = 0)."""
 import numpy as np
 import pytest
 import torch
@@ -25,6 +26,7 @@ def _dev(x):
     (gs.R_16F, 100, 60, 40, 1, 3, False, -1),       # CUDA-core fallback (misaligned leading dimension)
     (gs.R_16F, 64, 64, 0, 1, 0, False, -1),         # k == 0: beta only
     (gs.R_32F, 1024, 512, 1100, 1, 0, False, -1),   # FAST_TF32: split kernels + chunked kind::tf32 GEMM
+    (gs.R_32F, 1600, 1100, 1030, 2, 0, False, -1),  # FFMA stream-K (234 tiles on 296 slots): workspace, counters
 ])
 def test_graph_replay_matches_direct_call(dt, m, n, k, batch, lda_pad, ptr, algo):
     rng = np.random.default_rng(m + n + k)
@@ -56,7 +58,7 @@ def test_graph_replay_matches_direct_call(dt, m, n, k, batch, lda_pad, ptr, algo
 
     direct = C0.clone()
     with torch.cuda.stream(stream):
-        call(direct)                                   # warm-up: attributes, tensor-map buffer
+        call(direct)                                   # warm-up: attributes, tensor-map buffer, workspaces
     stream.synchronize()
     captured = C0.clone()
     if ptr:
