@@ -546,11 +546,15 @@ def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str
         line["allgather"] = {"ms": round(gms, 3), "bytes_per_rank": nbytes, "backend": "nccl",
                              "algbw_gbs": round(nbytes * (world - 1) / world / (gms * 1e-3) / 1e9, 1)}
         del full
-    if args.cublas and rank == 0:
-        line["cublas"] = cublas_compare(cfg, A, B, args.steps, args.warmup)
-        if "ms" in line["cublas"]:
-            # the reference's shader_cublas_ratio (bench/gemm_perf.zig:206): our ms / cuBLAS ms, same rank-0 shard
-            line["shader_cublas_ratio"] = round(max_kernel_ms / line["cublas"]["ms"], 4)
+    if args.cublas:
+        # Every rank runs cuBLAS on its own shard, so that all GPUs carry the same work (and heat) into the
+        # next item; rank 0's result is reported.
+        cub = cublas_compare(cfg, A, B, args.steps, args.warmup)
+        if rank == 0:
+            line["cublas"] = cub
+            if "ms" in cub:
+                # the reference's shader_cublas_ratio (bench/gemm_perf.zig:206): our ms / cuBLAS ms, rank-0 shard
+                line["shader_cublas_ratio"] = round(max_kernel_ms / cub["ms"], 4)
     del A, B, C, flush
     return line
 
