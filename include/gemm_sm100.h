@@ -126,7 +126,8 @@ enum {
     GS_KERNEL_FFMA = 1u << 3,     /* register-blocked FFMA sgemm */
     GS_KERNEL_SIMT = 1u << 4,     /* generic CUDA-core kernel for operands TMA cannot address */
     GS_KERNEL_SCALE = 1u << 5,    /* C = beta*C for k == 0 */
-    GS_KERNEL_TMAP = 1u << 6,     /* device-side tensor-map builder (pointer-array batches) */
+    GS_KERNEL_TMAP = 1u << 6,     /* device-side tensor-map builder (pointer-array batches above
+                                     GS_PTR_MAPS_IN_KERNEL_MAX_BATCH entries) */
     GS_KERNEL_TC_TF32 = 1u << 7   /* COMPUTE_32F_FAST_TF32: operand split + tcgen05 kind::tf32 */
 };
 
@@ -184,7 +185,13 @@ gs_status gs_gemm_strided_batched_ex(gs_handle handle, int transa, int transb, i
 /* Pointer-array batched typed GEMM; Aarray/Barray/Carray are DEVICE arrays of
  * device pointers, as with cuBLAS. Replaces cublas.gemmBatchedEx
  * (src/cublas.zig:239-241, RawGemmBatchedExDesc :268-288) behind
- * gemm.gemmBatchedEx (src/gemm.zig:636-663). */
+ * gemm.gemmBatchedEx (src/gemm.zig:636-663). Tensor-core calls of at most
+ * GS_PTR_MAPS_IN_KERNEL_MAX_BATCH entries are one launch: each CTA of the GEMM
+ * kernel writes the per-entry tensor maps it uses into its own slots of the
+ * handle's map buffer (3 * SMs * batchCount maps). Larger batches launch a map
+ * builder (GS_KERNEL_TMAP) first. */
+#define GS_PTR_MAPS_IN_KERNEL_MAX_BATCH 64
+
 gs_status gs_gemm_batched_ex(gs_handle handle, int transa, int transb, int m, int n, int k,
                              const void *alpha, const void *const Aarray[], int Atype, int lda,
                              const void *const Barray[], int Btype, int ldb, const void *beta,

@@ -108,6 +108,8 @@ struct TcArgs {
     const uint32_t *skip_flag;   // pointer-array batches: == skip_gen when a pointer is not 16-byte aligned
     uint32_t skip_gen;
     const CUtensorMap *c_maps;   // pointer-array batches with TMA-stored C: per-batch C maps in global memory
+    CUtensorMap *cta_maps;       // small pointer-array batches: per-CTA map slots (3 x batch each) that every CTA
+                                 // fills itself from the templates tmA/tmB/tmC and args.fb's pointer arrays
     const uint32_t *c_skip_flag; // == skip_gen when a C pointer is not 16-byte aligned (C then stored directly)
     int tma_store;               // epilogue writes C with TMA tensor stores (beta == 0, C TMA-addressable)
     int ab_evict_last;           // operand loads use the evict_last L2 policy
@@ -174,12 +176,49 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
 
     grid_dep_wait();
     grid_dep_launch();
-    // Pointer-array batches whose pointers TMA cannot address: every CTA reads
-    // the same word and, instead of the tensor-core pipeline, runs the CUDA-core
+    const CUtensorMap *a_maps = args.a_maps, *b_maps = args.b_maps, *c_maps = args.c_maps;
+    // TMA-stored C; pointer-array batches fall back to direct stores when a C entry is misaligned.
+    bool c_tma = args.tma_store && !(args.c_skip_flag != nullptr && *args.c_skip_flag == args.skip_gen);
+    // Pointer-array batches whose pointers TMA cannot address: every CTA sees
+    // the same answer and, instead of the tensor-core pipeline, runs the CUDA-core
     // tile loop over the whole batch (both CTAs of a pair take the same path,
     // before any cluster barrier or TMEM allocation).
     if constexpr (!WIDE && IN != IN_TF32) {  // pointer-array batches never use the wide tile or tf32
-        if (args.skip_flag != nullptr && *args.skip_flag == args.skip_gen) {
+        if (args.cta_maps != nullptr) {
+            // Small batches, one launch: the CTA checks every entry's pointers, then writes the maps it
+            // uses into its own slots -- the template with the entry's address swapped in by
+            // tensormap.replace -- and releases them to the tensor-map proxy; the threads that issue TMA
+            // through a map acquire it first. Slots are private to the CTA, so no CTA waits for another.
+            bool bad_ab = false, bad_c = false;
+            for (int i = threadIdx.x; i < args.batch; i += blockDim.x) {
+                const uint64_t pa = reinterpret_cast<uint64_t>(args.fb.a_arr[i]);
+                const uint64_t pb = reinterpret_cast<uint64_t>(args.fb.b_arr[i]);
+                bad_ab |= ((pa | pb) & 15u) != 0u;
+                if (args.tma_store) bad_c |= (reinterpret_cast<uint64_t>(args.fb.c_arr[i]) & 15u) != 0u;
+            }
+            bad_ab = __syncthreads_or(bad_ab) != 0;
+            bad_c = __syncthreads_or(bad_c) != 0;
+            if (bad_ab) {
+                simt::simt_tiles<IN, OUT>(args.fb, blockIdx.x, gridDim.x, smem);
+                return;
+            }
+            c_tma = args.tma_store && !bad_c;
+            CUtensorMap *own = args.cta_maps + static_cast<size_t>(blockIdx.x) * 3u * static_cast<size_t>(args.batch);
+            for (int i = threadIdx.x; i < args.batch; i += blockDim.x) {
+                own[i] = tmA;
+                tensormap_set_address(own + i, args.fb.a_arr[i]);
+                own[args.batch + i] = tmB;
+                tensormap_set_address(own + args.batch + i, args.fb.b_arr[i]);
+                if (c_tma) {
+                    own[2 * args.batch + i] = tmC;
+                    tensormap_set_address(own + 2 * args.batch + i, args.fb.c_arr[i]);
+                }
+            }
+            tensormap_release();
+            a_maps = own;
+            b_maps = own + args.batch;
+            c_maps = c_tma ? own + 2 * args.batch : nullptr;
+        } else if (args.skip_flag != nullptr && *args.skip_flag == args.skip_gen) {
             simt::simt_tiles<IN, OUT>(args.fb, blockIdx.x, gridDim.x, smem);
             return;
         }
@@ -198,7 +237,7 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
         mbar_init(drain, 1);
         fence_barrier_init();
     }
-    if (warp == 0 && lane == 0 && args.a_maps == nullptr) {
+    if (warp == 0 && lane == 0 && a_maps == nullptr) {
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
     }
@@ -236,9 +275,9 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
                 const int n0 = nb * TILE_N + static_cast<int>(rank) * C_::B_BOX;
                 const CUtensorMap *ma = &tmA, *mbp = &tmB;
                 int ab = args.a_bcast ? 0 : b, bb = args.b_bcast ? 0 : b;
-                if (args.a_maps != nullptr) {
-                    ma = args.a_maps + b;
-                    mbp = args.b_maps + b;
+                if (a_maps != nullptr) {
+                    ma = a_maps + b;
+                    mbp = b_maps + b;
                     ab = 0;
                     bb = 0;
                     tensormap_acquire(ma);
@@ -434,8 +473,6 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
         const int row = quad * 32 + lane;
         const uint32_t tempty_leader = CG == 2 ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
         const uint64_t pol_c = l2_policy_evict_first();
-        // TMA-stored C; pointer-array batches fall back to direct stores when a C entry is misaligned.
-        const bool c_tma = args.tma_store && !(args.c_skip_flag != nullptr && *args.c_skip_flag == args.skip_gen);
         int stg_flip = 0;
         int it = 0;
         uint32_t echunks = 0;  // CHUNKED: accumulator fills consumed so far
@@ -487,9 +524,9 @@ __global__ void __launch_bounds__(Cfg<CG, WIDE>::THREADS, 1)
             if (args.c_arr != nullptr) Cb = args.c_arr[b];
             else Cb = static_cast<uint8_t *>(args.C) + static_cast<size_t>(b) * args.stride_c *
                                                         ((OUT == OUT_F16 || OUT == OUT_BF16) ? 2 : 4);
-            const CUtensorMap *cmap = args.c_maps != nullptr ? args.c_maps + b : &tmC;
-            const int cz = args.c_maps != nullptr ? 0 : b;
-            if (c_tma && args.c_maps != nullptr && lane == 0) tensormap_acquire(cmap);
+            const CUtensorMap *cmap = c_maps != nullptr ? c_maps + b : &tmC;
+            const int cz = c_maps != nullptr ? 0 : b;
+            if (c_tma && c_maps != nullptr && lane == 0) tensormap_acquire(cmap);
             // One pass per accumulator slot this tile owns: the tile's 256-column
             // buffer, or (WIDE) each half of the 512-column accumulator in turn.
 #pragma unroll 1
@@ -610,8 +647,7 @@ __global__ void k_build_ptr_maps(const CUtensorMap tmpl_a, const CUtensorMap tmp
             atomicExch(misaligned_c, gen);
         } else {
             maps_c[i] = tmpl_c;
-            asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;"
-                         ::"l"(reinterpret_cast<uint64_t>(maps_c + i)), "l"(pc) : "memory");
+            tensormap_set_address(maps_c + i, c_arr[i]);
         }
     }
     const uint64_t pa = reinterpret_cast<uint64_t>(a_arr[i]), pb = reinterpret_cast<uint64_t>(b_arr[i]);
@@ -621,11 +657,9 @@ __global__ void k_build_ptr_maps(const CUtensorMap tmpl_a, const CUtensorMap tmp
     }
     maps_a[i] = tmpl_a;
     maps_b[i] = tmpl_b;
-    asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;"
-                 ::"l"(reinterpret_cast<uint64_t>(maps_a + i)), "l"(pa) : "memory");
-    asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;"
-                 ::"l"(reinterpret_cast<uint64_t>(maps_b + i)), "l"(pb) : "memory");
-    asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
+    tensormap_set_address(maps_a + i, a_arr[i]);
+    tensormap_set_address(maps_b + i, b_arr[i]);
+    tensormap_release();
 }
 
 // Largest number of co-resident CTA pairs for one 2-SM kernel instantiation on this device.
@@ -670,6 +704,7 @@ static cudaError_t launch_kernel(Context &ctx, const CUtensorMap &ta, const CUte
     if constexpr (CG == 2) {
         const long long mp = max_pairs<IN, OUT, CG, WIDE>(ctx);
         const long long pairs = args.total_tiles < mp ? args.total_tiles : mp;
+        if (args.cta_maps != nullptr && 2 * pairs > ctx.sm_count) return cudaErrorInvalidConfiguration;  // slots per CTA
         e = launch_pdl(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(C_::THREADS), C_::SMEM, ctx.stream, 2, ta,
                        tb, tcm, args);
         ctx.launches++;
@@ -886,9 +921,15 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     const int cg = shape == 1 ? 1 : 2;
     TcArgs args = make_args(ctx, d, shape);
     // Template maps over a placeholder (16-byte aligned, never dereferenced
-    // through the template) with the per-batch geometry; the builder kernel
-    // swaps in each batch entry's address.
-    const size_t need = 3 * static_cast<size_t>(d.batch) * sizeof(CUtensorMap);
+    // through the template) with the per-batch geometry; each batch entry's
+    // address is swapped in on the device. Small batches (and a handle that
+    // may allocate) do that inside the GEMM kernel, one launch: every CTA fills
+    // its own 3 x batch slots (the grid never exceeds the SM count). Larger
+    // batches run the builder kernel first, which fills 3 x batch slots once.
+    const bool in_kernel = ctx.may_allocate && d.batch <= GS_PTR_MAPS_IN_KERNEL_MAX_BATCH;
+    const size_t slots = in_kernel ? static_cast<size_t>(ctx.sm_count) * static_cast<size_t>(d.batch)
+                                   : static_cast<size_t>(d.batch);
+    const size_t need = 3 * slots * sizeof(CUtensorMap);
     if (ctx.tmap_bytes < need) {
         // Grow-only, checked before anything of this call is enqueued. The old buffer may still be read
         // by kernels in flight, so it is not freed here (cudaFree would synchronise the device): it is
@@ -925,6 +966,14 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     dc.C = ctx.tmap_buf;
     const bool c_tma = make_c_map(dc, &tcm);
     args.tma_store = c_tma ? 1 : 0;
+    args.a_bcast = 1;
+    args.b_bcast = 1;
+    args.c_arr = c_arr;
+    args.fb = simt::make_args(d, a_arr, b_arr, c_arr);
+    if (in_kernel) {
+        args.cta_maps = static_cast<CUtensorMap *>(ctx.tmap_buf);
+        return dispatch_shape(shape, ctx, d, ta, tb, tcm, args);
+    }
     CUtensorMap *maps_a = static_cast<CUtensorMap *>(ctx.tmap_buf);
     CUtensorMap *maps_b = maps_a + d.batch;
     CUtensorMap *maps_c = c_tma ? maps_b + d.batch : nullptr;
@@ -938,16 +987,12 @@ cudaError_t launch_tc_ptr_array(Context &ctx, const GemmDesc &d, const void *con
     ctx.launches++;
     ctx.last_kernels |= GS_KERNEL_TMAP;
     if (e != cudaSuccess) return e;
-    args.a_bcast = 1;
-    args.b_bcast = 1;
     args.a_maps = maps_a;
     args.b_maps = maps_b;
-    args.c_arr = c_arr;
     args.skip_flag = misaligned;
     args.skip_gen = gen;
     args.c_maps = maps_c;
     args.c_skip_flag = c_tma ? misaligned_c : nullptr;
-    args.fb = simt::make_args(d, a_arr, b_arr, c_arr);
     return dispatch_shape(shape, ctx, d, ta, tb, tcm, args);
 }
 

@@ -145,8 +145,22 @@ __device__ __forceinline__ void bulk_wait_group_read() {
 // Wait until every committed bulk group has completed (writes visible).
 __device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Orders a tensor map written in global memory by an earlier kernel before its
-// use by the tensor-map proxy (TMA).
+// Swaps the global address of a tensor map held in global memory (the map's
+// other fields stay as encoded on the host).
+__device__ __forceinline__ void tensormap_set_address(CUtensorMap *map, const void *addr) {
+    asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "l"(reinterpret_cast<uint64_t>(addr)) : "memory");
+}
+
+// Releases this thread's earlier writes of tensor maps to the tensor-map proxy
+// (pairs with tensormap_acquire by the thread that issues TMA through them).
+__device__ __forceinline__ void tensormap_release() {
+    asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
+}
+
+// Orders a tensor map written in global memory (by an earlier kernel, or by
+// another thread of this CTA before a barrier) before its use by the
+// tensor-map proxy (TMA).
 __device__ __forceinline__ void tensormap_acquire(const CUtensorMap *map) {
     asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -52,6 +52,7 @@ KERNEL_TC_TF32 = 1 << 7
 
 ELEM_SIZE = {R_32F: 4, R_64F: 8, R_16F: 2, R_8I: 1, R_32I: 4, R_16BF: 2}
 NOALLOC_MAX_BATCH = 256  # GS_NOALLOC_MAX_BATCH
+PTR_MAPS_IN_KERNEL_MAX_BATCH = 64  # GS_PTR_MAPS_IN_KERNEL_MAX_BATCH
 
 
 class GemmError(RuntimeError):

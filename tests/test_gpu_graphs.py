@@ -75,9 +75,10 @@ def test_graph_replay_matches_direct_call(dt, m, n, k, batch, lda_pad, ptr, algo
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(captured, direct)
-    # replaying again applies the GEMM again on top (beta != 0): same as a second direct call
-    g.replay()
+    # replaying again applies the GEMM again on top (beta != 0): same as a second direct call. The replay
+    # goes on the handle's stream, ordered before the direct call: both use the handle's workspaces.
     with torch.cuda.stream(stream):
+        g.replay()
         call(direct)
     torch.cuda.synchronize()
     assert torch.equal(captured, direct)

@@ -292,7 +292,54 @@ def test_pointer_array_batched(handle, dt, misalign, algo):
     if dt == gs.R_32F:
         assert kern & gs.KERNEL_FFMA
     else:
-        assert kern & gs.KERNEL_TMAP and kern & TC[dt]
+        # up to PTR_MAPS_IN_KERNEL_MAX_BATCH entries the GEMM kernel builds its own maps: no builder launch
+        assert kern & TC[dt] and not kern & gs.KERNEL_TMAP
+    assert handle.device_error() == 0
+
+
+@pytest.mark.parametrize("dt", [gs.R_16F, gs.R_8I])
+@pytest.mark.parametrize("batch", [gs.PTR_MAPS_IN_KERNEL_MAX_BATCH, gs.PTR_MAPS_IN_KERNEL_MAX_BATCH + 6])
+@pytest.mark.parametrize("beta,misalign", [(0.5, None), (0.0, None), (0.0, "c"), (0.5, "a")])
+@pytest.mark.parametrize("algo", TILES)
+def test_pointer_array_map_paths(handle, dt, batch, beta, misalign, algo):
+    """Both ways of building the per-entry tensor maps of a pointer-array call, against the oracle: at the
+    in-kernel limit (one launch; each CTA writes its own maps) and past it (the map builder, then the GEMM: two
+    launches), with TMA-stored C (beta 0), a misaligned C entry (direct stores), a misaligned A entry (CUDA-core
+    fallback for the whole batch) and directly stored C (beta != 0). Ragged M and N."""
+    import torch
+
+    rng = np.random.default_rng(70 + dt + batch + algo + (misalign == "c") + 2 * (misalign == "a") + int(4 * beta))
+    m, n, k = 144, 72, 64  # leading dimensions TMA can address for every type (16-byte multiples)
+    ct = OUT_OF[dt]
+    es_a, es_c = np.dtype(NP_OF[dt]).itemsize, np.dtype(NP_OF[ct]).itemsize
+    a_list = [make_input(rng, m * k + 8, dt) for _ in range(batch)]
+    b_list = [make_input(rng, k * n, dt) for _ in range(batch)]
+    c_list = [make_c(rng, m * n + 8, ct) for _ in range(batch)]
+    da, db, dc = [to_dev(x) for x in a_list], [to_dev(x) for x in b_list], [to_dev(x) for x in c_list]
+    bad = batch - 3  # the entry whose A or C pointer is off by one element
+    sa = [1 if misalign == "a" and j == bad else 0 for j in range(batch)]
+    sc = [1 if misalign == "c" and j == bad else 0 for j in range(batch)]
+    aptr = torch.tensor([t.data_ptr() + sa[j] * es_a for j, t in enumerate(da)], dtype=torch.int64, device="cuda")
+    bptr = torch.tensor([t.data_ptr() for t in db], dtype=torch.int64, device="cuda")
+    cptr = torch.tensor([t.data_ptr() + sc[j] * es_c for j, t in enumerate(dc)], dtype=torch.int64, device="cuda")
+    alpha = 2.0 if dt == gs.R_8I else 0.75
+    if dt == gs.R_8I and beta != 0.0:
+        beta = -1.0  # COMPUTE_32I scalars are int32 (gemmEx's alpha/beta pointers)
+    n0 = handle.launch_count()
+    handle.gemm_batched_ex(0, 0, m, n, k, alpha, aptr, dt, m, bptr, dt, k, beta, cptr, ct, m, batch, COMPUTE[dt],
+                           algo=algo)
+    launched, kern = handle.launch_count() - n0, handle.last_kernels()
+    refs = [x.copy() for x in c_list]
+    views = [r[sc[j]:sc[j] + m * n] for j, r in enumerate(refs)]
+    a_view = [x[sa[j]:sa[j] + m * k].copy() for j, x in enumerate(a_list)]
+    assert orc.gemm_batched_ex(0, 0, m, n, k, alpha, a_view, dt, m, b_list, dt, k, beta, views, ct, m,
+                               compute_type=COMPUTE[dt]) == orc.OK
+    for j in range(batch):
+        assert_parity(to_host(dc[j]), refs[j], ct, dt if dt != gs.R_8I else gs.R_32F)
+    in_kernel = batch <= gs.PTR_MAPS_IN_KERNEL_MAX_BATCH
+    assert kern & TC[dt]
+    assert bool(kern & gs.KERNEL_TMAP) == (not in_kernel)
+    assert launched == (1 if in_kernel else 2)
     assert handle.device_error() == 0
 
 
@@ -475,4 +522,5 @@ def test_sgemm_stream_k(handle, m, n, k, batch, pad, op_a, op_b):
     for rep in range(2):
         run_case(handle, gs.R_32F, op_a, op_b, m, n, k, alpha=1.5, beta=-0.5, pad=pad, batch=batch,
                  seed=m + n + k + rep, expect_kernel=gs.KERNEL_FFMA)
+
 
