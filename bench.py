@@ -549,7 +549,7 @@ def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str
     if args.cublas:
         # Every rank runs cuBLAS on its own shard, so that all GPUs carry the same work (and heat) into the
         # next item; rank 0's result is reported.
-        cub = cublas_compare(cfg, A, B, args.steps, args.warmup)
+        cub = cublas_compare(cfg, A, B, args.steps, args.warmup, flush)
         if rank == 0:
             line["cublas"] = cub
             if "ms" in cub:
@@ -559,9 +559,11 @@ def run_ours_one(args, h, stream, peaks, rank, world, local, dist, cfg_name: str
     return line
 
 
-def cublas_compare(cfg: dict, A, B, steps: int, warmup: int) -> dict:
+def cublas_compare(cfg: dict, A, B, steps: int, warmup: int, flush=None) -> dict:
     """cuBLAS on the same operands and arguments (cublasGemmEx / cublasGemmStridedBatchedEx, as
-    slang-gemm's src/cublas.zig calls them), timed like our kernel, for shader_cublas_ratio."""
+    slang-gemm's src/cublas.zig calls them), timed like our kernel, for shader_cublas_ratio: back to back
+    when the operands are larger than L2, else with `flush` (the same 256 MiB buffer) written before every
+    call and each call timed on its own."""
     import torch
 
     import cublas_ref
@@ -581,16 +583,27 @@ def cublas_compare(cfg: dict, A, B, steps: int, warmup: int) -> dict:
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        fn()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    if flush is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+    else:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for s0, s1 in evs:
+            flush.zero_()
+            s0.record(stream)
+            fn()
+            s1.record(stream)
+        torch.cuda.synchronize()
+        ms = sum(s0.elapsed_time(s1) for s0, s1 in evs) / max(1, steps)
     cb.close()
     unit = "TOP/s" if cfg["dt"] == 3 else "TFLOP/s"
     return {"ms": round(ms, 4), "value": round(2.0 * m * n * k * b / ms / 1e9, 1), "unit": unit,
+            "l2": "inputs larger than L2" if flush is None else "flushed before every call, as ours",
             "call": "cublasGemmStridedBatchedEx" if b > 1 else "cublasGemmEx",
             "version": cublas_ref.version_string()}
 
