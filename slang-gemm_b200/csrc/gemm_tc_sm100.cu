@@ -837,33 +837,27 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int shape) {
     return a;
 }
 
-// Share of a persistent pair launch's tile slots that hold output: tiles of
-// 256 x tile_n run in rounds of `pairs`, the last round partly idle, edge
-// tiles partly outside C.
-static double slot_use(const GemmDesc &d, int tile_n, long long pairs, long long *rounds) {
-    const long long tiles = static_cast<long long>((d.m + 2 * BM - 1) / (2 * BM)) * ((d.n + tile_n - 1) / tile_n) * d.batch;
-    *rounds = (tiles + pairs - 1) / pairs;
-    return static_cast<double>(d.m) * d.n * d.batch / (static_cast<double>(*rounds) * pairs * 2 * BM * tile_n);
-}
-
 // Tile-shape choice. The algo argument is honoured as a hint
 // (CUBLAS_GEMM_ALGO0 = 1-SM 128 x 256 tile, ALGO1 = 2-SM 256 x 256 pair tile,
-// ALGO2 = 2-SM 256 x 512 wide pair tile); any other value picks the pair tile
-// whenever M > 128 gives both CTAs rows, and the wide pair tile when the
-// problem has more than one 256-column block and either a K loop long enough
-// (>= 32 stages) to amortise the undoubled accumulator's drain, or an
-// arithmetic intensity below the B200's tensor / HBM ridge (~260 flop/byte
-// for 16-bit inputs, ~520 op/byte for INT8), where the wide tile's smaller
-// operand traffic is worth more than the drain it exposes. For 16-bit inputs
-// above the ridge with a short K loop the wide tile still wins (1-3 %) once
-// the launch runs at least four rounds of wide tiles over the SM pairs and
-// its last round leaves no more slots idle than the pair tile's (measured:
-// batch-4 4096x4096x1024 FP16 0.122 -> 0.118 ms, batch-9/11/13
-// 2048x2048x1536 0.095/0.116/0.135 -> 0.093/0.113/0.134); where it fills its
-// last round worse (batch-8 2048x2048x1536 FP16 0.085 -> 0.093) the pair tile
-// stays. INT8 takes the wide tile there only for long persistent runs (at
-// least 16 rounds of wide tiles): batch-9/11/13 2048^3 (4-6 rounds) ran 3-4 %
-// slower on it, batch-64 2048^3 (C5b, 28 rounds) 1-4 % faster on three boxes.
+// ALGO2 = 2-SM 256 x 512 wide pair tile). Otherwise, from a timed sweep of
+// every tile over 36 shapes x FP16 / INT8 (single GEMMs 1024^3 .. 16384 x 4096,
+// K 256 .. 16384, batches of 8 .. 256):
+//  - the persistent kernel runs its tiles in rounds over the resident CTAs
+//    (148 one-SM CTAs or 74 pairs), so a shape costs about
+//    rounds x (work per SM per tile) / (the tile's throughput): 128 x 256 x K
+//    per SM for the 1-SM and pair tiles, 128 x 512 x K for the wide tile, at
+//    throughputs 0.86 / 0.91 / 1 of the wide tile's (measured at 8192^3); the
+//    cheapest wins;
+//  - when every 1-SM tile fits in one round the 1-SM tile is taken: it then
+//    ran 1-7 % ahead of the pair tile and up to 1.7x ahead of the wide one
+//    (1024^3, 2048^3, 512 x 512 x 16384);
+//  - with at most 4 K stages the call is all epilogue and the wide tile, whose
+//    16 epilogue warps drain C fastest, is taken (INT8 8192 x 4096 x 256:
+//    1.3x ahead of the pair tile).
+// Against the earlier rule (wide tile for >= 32 K stages or below the
+// tensor / HBM ridge) this took the sweep's geometric-mean loss against the
+// best tile from 9.7 % to 0.4 %; every configuration of the north star keeps
+// the wide tile.
 static int choose_shape_any(const GemmDesc &d, long long pairs);
 static int choose_shape(const Context &ctx, const GemmDesc &d) {
     const int shape = choose_shape_any(d, ctx.sm_count >= 2 ? ctx.sm_count / 2 : 1);
@@ -877,22 +871,20 @@ static int choose_shape_any(const GemmDesc &d, long long pairs) {
     if (d.algo == 1) return 2;
     if (d.algo == 2) return 3;
     if (d.m <= BM) return 1;
-    if (d.n <= BN) return 2;
-    const double es = static_cast<double>(in_elem_size(d.in_kind));
-    const int k_blocks = (d.k + BK_BYTES / static_cast<int>(es) - 1) / (BK_BYTES / static_cast<int>(es));
-    if (k_blocks >= 32) return 3;
-    const double m = d.m, n = d.n, k = d.k;
-    const double flops = 2.0 * m * n * k;
-    const double bytes = m * k * es + k * n * es + m * n * static_cast<double>(out_elem_size(d.out_kind)) *
-                                                        (d.ep.beta_zero ? 1.0 : 2.0);
-    const double ridge = d.in_kind == IN_I8 ? 520.0 : 260.0;
-    if (flops / bytes < ridge) return 3;
-    long long rounds_wide = 0, rounds_pair = 0;
-    const double use_wide = slot_use(d, 2 * BN, pairs, &rounds_wide);
-    if (d.in_kind == IN_I8) return rounds_wide >= 16 ? 3 : 2;
-    if (d.in_kind != IN_F16 && d.in_kind != IN_BF16) return 2;
-    const double use_pair = slot_use(d, BN, pairs, &rounds_pair);
-    return rounds_wide >= 4 && use_wide >= use_pair - 1e-3 ? 3 : 2;
+    auto cdiv = [](long long x, long long y) { return (x + y - 1) / y; };
+    const long long mb1 = cdiv(d.m, BM), mb2 = cdiv(d.m, 2 * BM);
+    const long long t1 = mb1 * cdiv(d.n, BN) * d.batch;       // 128 x 256 tiles
+    const long long t2 = mb2 * cdiv(d.n, BN) * d.batch;       // 256 x 256 pair tiles
+    const long long t3 = mb2 * cdiv(d.n, 2 * BN) * d.batch;   // 256 x 512 wide tiles
+    const long long r1 = cdiv(t1, 2 * pairs), r2 = cdiv(t2, pairs), r3 = cdiv(t3, pairs);
+    if (r1 == 1) return 1;
+    const int es = static_cast<int>(in_elem_size(d.in_kind));
+    const int k_blocks = static_cast<int>(cdiv(d.k, BK_BYTES / es));
+    if (d.n > BN && k_blocks <= 4) return 3;
+    const double c1 = static_cast<double>(r1) / 0.86, c2 = static_cast<double>(r2) / 0.91;
+    const double c3 = 2.0 * static_cast<double>(r3);
+    if (c3 <= c2 && c3 <= c1) return 3;
+    return c1 < c2 ? 1 : 2;
 }
 
 }  // namespace tc
