@@ -128,7 +128,8 @@ enum {
     GS_KERNEL_SCALE = 1u << 5,    /* C = beta*C for k == 0 */
     GS_KERNEL_TMAP = 1u << 6,     /* device-side tensor-map builder (pointer-array batches above
                                      GS_PTR_MAPS_IN_KERNEL_MAX_BATCH entries) */
-    GS_KERNEL_TC_TF32 = 1u << 7   /* COMPUTE_32F_FAST_TF32: operand split + tcgen05 kind::tf32 */
+    GS_KERNEL_TC_TF32 = 1u << 7,  /* COMPUTE_32F_FAST_TF32: operand split + tcgen05 kind::tf32 */
+    GS_KERNEL_REDUCE = 1u << 8    /* split-K: sum of the tensor-core kernel's per-slice partials, alpha/beta */
 };
 
 /* ---------------------------------------------------------------------- */

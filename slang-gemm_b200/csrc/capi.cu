@@ -192,6 +192,7 @@ gs_status gs_destroy(gs_handle h) {
     if (h->ctx.tmap_buf) cudaFree(h->ctx.tmap_buf);
     if (h->ctx.sk_buf) cudaFree(h->ctx.sk_buf);
     if (h->ctx.sk_counts) cudaFree(h->ctx.sk_counts);
+    if (h->ctx.splitk_buf) cudaFree(h->ctx.splitk_buf);
     for (void *p : h->ctx.retired) cudaFree(p);
     if (h->ctx.tf32_buf) cudaFree(h->ctx.tf32_buf);
     if (h->ctx.h2d) cudaStreamDestroy(h->ctx.h2d);

@@ -889,7 +889,116 @@ static int choose_shape_any(const GemmDesc &d, long long pairs) {
 
 }  // namespace tc
 
+namespace tc {
+
+// Split-K reduction: C = alpha * (sum over the K slices' partial results, in slice order) + beta * C, with the
+// epilogue rounding of every other path. Partial slice s of element (row, col) is ws[s * m * n + col * m + row].
+template <int OUT>
+__global__ void k_splitk_reduce(const void *ws, int parts, int m, int n, void *C, long long ldc, Epilogue ep) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const size_t mn = static_cast<size_t>(m) * static_cast<size_t>(n);
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < mn;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t col = i / static_cast<size_t>(m), row = i - col * static_cast<size_t>(m);
+        const size_t dst = row + col * static_cast<size_t>(ldc);
+        if constexpr (OUT == OUT_I32) {
+            const int32_t *p = static_cast<const int32_t *>(ws) + i;
+            int32_t acc = 0;  // |sum| <= 128 * 128 * K < 2^31 (K is checked on entry)
+            for (int s = 0; s < parts; ++s) acc += __ldcs(p + static_cast<size_t>(s) * mn);
+            store_iacc(C, dst, acc, ep);
+        } else {
+            const float *p = static_cast<const float *>(ws) + i;
+            float acc = 0.0f;
+            for (int s = 0; s < parts; ++s) acc = __fadd_rn(acc, __ldcs(p + static_cast<size_t>(s) * mn));
+            store_facc<OUT>(C, dst, acc, ep);
+        }
+    }
+}
+
+// K slices for a single GEMM whose 128 x 256 tiles fill less than half the SMs but whose K loop is long:
+// the largest power of two S <= 32 that divides the K stages, leaves every slice >= 16 stages and keeps
+// S x tiles within the SM count. 1 = no split. The slices run as a strided batch of the tensor-core kernel
+// into a handle workspace of S partial C (f32, or s32 for INT8), then k_splitk_reduce adds them in order.
+// 512 x 512 x 16384: 8 tiles on 148 SMs become 16 slices x 8 tiles.
+static int splitk_parts(const Context &ctx, const GemmDesc &d) {
+    if (d.batch != 1 || d.algo >= 0 || d.in_kind == IN_TF32 || !ctx.may_allocate || d.m <= BM) return 1;
+    const int bk = BK_BYTES / static_cast<int>(in_elem_size(d.in_kind));
+    if (d.k % bk != 0) return 1;
+    const long long kb = d.k / bk;
+    const long long tiles = static_cast<long long>((d.m + BM - 1) / BM) * ((d.n + BN - 1) / BN);
+    const long long sms = ctx.sm_count > 0 ? ctx.sm_count : 148;
+    if (2 * tiles > sms) return 1;
+    int s = 1;
+    while (s < 32 && 2 * s * tiles <= sms && kb % (2 * s) == 0 && kb / (2 * s) >= 16) s *= 2;
+    return s;
+}
+
+}  // namespace tc
+
+static cudaError_t launch_tc_one(Context &ctx, const GemmDesc &d);
+
 cudaError_t launch_tc(Context &ctx, const GemmDesc &d) {
+    using namespace tc;
+    const int parts = splitk_parts(ctx, d);
+    if (parts == 1) return launch_tc_one(ctx, d);
+    const size_t es_p = 4;  // f32 or s32 partials
+    const size_t mn = static_cast<size_t>(d.m) * static_cast<size_t>(d.n);
+    const size_t need = mn * static_cast<size_t>(parts) * es_p;
+    if (ctx.splitk_bytes < need) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(ctx.stream, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone) {
+            ctx.last_error = "the split-K workspace must grow, which cannot be captured: make one call of this "
+                             "size before the stream capture";
+            return cudaErrorStreamCaptureUnsupported;
+        }
+        const size_t bytes = need > 2 * ctx.splitk_bytes ? need : 2 * ctx.splitk_bytes;
+        void *grown = nullptr;
+        const cudaError_t e = cudaMalloc(&grown, bytes);
+        if (e == cudaErrorMemoryAllocation) {
+            cudaGetLastError();
+            return launch_tc_one(ctx, d);  // no room: the unsplit launch needs no workspace
+        }
+        if (e != cudaSuccess) return e;
+        if (ctx.splitk_buf) ctx.retired.push_back(ctx.splitk_buf);  // kernels in flight may still use it
+        ctx.splitk_buf = grown;
+        ctx.splitk_bytes = bytes;
+    }
+    // The slices as a strided batch: slice s reads K elements [s*Ks, (s+1)*Ks) -- columns of a stored
+    // op-N A / op-T B, rows of an op-T A / op-N B -- and writes partial s, alpha 1, beta 0.
+    const long long ks = d.k / parts;
+    GemmDesc p = d;
+    p.k = static_cast<int>(ks);
+    p.batch = parts;
+    p.stride_a = d.trans_a ? ks : ks * d.lda;
+    p.stride_b = d.trans_b ? ks * d.ldb : ks;
+    p.out_kind = d.in_kind == IN_I8 ? OUT_I32 : OUT_F32;
+    p.C = ctx.splitk_buf;
+    p.ldc = d.m;
+    p.stride_c = static_cast<long long>(mn);
+    p.ep = Epilogue{1.0f, 0.0f, 1, 0, 1, 1};
+    cudaError_t e = launch_tc_one(ctx, p);
+    if (e != cudaSuccess) return e;
+    const int threads = 256;
+    const long long want = (static_cast<long long>(mn) + threads - 1) / threads;
+    const unsigned blocks = static_cast<unsigned>(want < 8LL * ctx.sm_count ? want : 8LL * ctx.sm_count);
+    switch (d.out_kind) {
+    case OUT_F32: e = launch_pdl(k_splitk_reduce<OUT_F32>, dim3(blocks), dim3(threads), 0, ctx.stream, 1,
+                                 static_cast<const void *>(ctx.splitk_buf), parts, d.m, d.n, d.C, d.ldc, d.ep); break;
+    case OUT_F16: e = launch_pdl(k_splitk_reduce<OUT_F16>, dim3(blocks), dim3(threads), 0, ctx.stream, 1,
+                                 static_cast<const void *>(ctx.splitk_buf), parts, d.m, d.n, d.C, d.ldc, d.ep); break;
+    case OUT_BF16: e = launch_pdl(k_splitk_reduce<OUT_BF16>, dim3(blocks), dim3(threads), 0, ctx.stream, 1,
+                                  static_cast<const void *>(ctx.splitk_buf), parts, d.m, d.n, d.C, d.ldc, d.ep); break;
+    case OUT_I32: e = launch_pdl(k_splitk_reduce<OUT_I32>, dim3(blocks), dim3(threads), 0, ctx.stream, 1,
+                                 static_cast<const void *>(ctx.splitk_buf), parts, d.m, d.n, d.C, d.ldc, d.ep); break;
+    default: return cudaErrorInvalidValue;
+    }
+    ctx.launches++;
+    ctx.last_kernels |= GS_KERNEL_REDUCE;
+    return e;
+}
+
+static cudaError_t launch_tc_one(Context &ctx, const GemmDesc &d) {
     using namespace tc;
     const int shape = choose_shape(ctx, d);
     const int cg = shape == 1 ? 1 : 2;

@@ -78,6 +78,9 @@ struct Context {
     size_t sk_bytes = 0;
     void *sk_counts = nullptr;
     size_t sk_count_bytes = 0;
+    // split-K workspace of the tensor-core path: one f32 / s32 partial C per K slice
+    void *splitk_buf = nullptr;
+    size_t splitk_bytes = 0;
     // false for contexts over caller-provided memory only (the no-allocation entry point)
     bool may_allocate = true;
     // split operands of the FAST_TF32 tensor-core path

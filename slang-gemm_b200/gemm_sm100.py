@@ -48,6 +48,7 @@ KERNEL_FFMA = 1 << 3
 KERNEL_SIMT = 1 << 4
 KERNEL_SCALE = 1 << 5
 KERNEL_TMAP = 1 << 6
+KERNEL_REDUCE = 1 << 8
 KERNEL_TC_TF32 = 1 << 7
 
 ELEM_SIZE = {R_32F: 4, R_64F: 8, R_16F: 2, R_8I: 1, R_32I: 4, R_16BF: 2}

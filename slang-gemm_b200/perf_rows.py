@@ -230,7 +230,7 @@ def run_case(case: mf.Case, h: gs.Handle, cb: cublas_ref.Cublas, warmup: int, it
 def gs_kernel_names(bits: int) -> list[str]:
     names = [(gs.KERNEL_TC_F16, "tc_f16"), (gs.KERNEL_TC_BF16, "tc_bf16"), (gs.KERNEL_TC_I8, "tc_i8"),
              (gs.KERNEL_FFMA, "ffma_f32"), (gs.KERNEL_SIMT, "simt"), (gs.KERNEL_SCALE, "scale"),
-             (gs.KERNEL_TMAP, "tmap_build")]
+             (gs.KERNEL_TMAP, "tmap_build"), (gs.KERNEL_TC_TF32, "tc_tf32"), (gs.KERNEL_REDUCE, "splitk_reduce")]
     return [n for b, n in names if bits & b]
 
 
