@@ -893,13 +893,43 @@ namespace tc {
 
 // Split-K reduction: C = alpha * (sum over the K slices' partial results, in slice order) + beta * C, with the
 // epilogue rounding of every other path. Partial slice s of element (row, col) is ws[s * m * n + col * m + row].
+// With M a multiple of 4 each thread takes four consecutive rows of one column: 16-byte loads of the partials.
 template <int OUT>
 __global__ void k_splitk_reduce(const void *ws, int parts, int m, int n, void *C, long long ldc, Epilogue ep) {
     grid_dep_wait();
     grid_dep_launch();
     const size_t mn = static_cast<size_t>(m) * static_cast<size_t>(n);
-    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < mn;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t first = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t step = static_cast<size_t>(gridDim.x) * blockDim.x;
+    if ((m & 3) == 0) {
+        const size_t q = mn / 4;
+        for (size_t v = first; v < q; v += step) {
+            const size_t i = 4 * v, col = i / static_cast<size_t>(m), row = i - col * static_cast<size_t>(m);
+            const size_t dst = row + col * static_cast<size_t>(ldc);
+            if constexpr (OUT == OUT_I32) {
+                const int4 *p = static_cast<const int4 *>(ws) + v;
+                int4 a = make_int4(0, 0, 0, 0);
+                for (int s = 0; s < parts; ++s) {
+                    const int4 t = __ldcs(p + static_cast<size_t>(s) * q);
+                    a.x += t.x; a.y += t.y; a.z += t.z; a.w += t.w;
+                }
+                store_iacc(C, dst, a.x, ep); store_iacc(C, dst + 1, a.y, ep);
+                store_iacc(C, dst + 2, a.z, ep); store_iacc(C, dst + 3, a.w, ep);
+            } else {
+                const float4 *p = static_cast<const float4 *>(ws) + v;
+                float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                for (int s = 0; s < parts; ++s) {
+                    const float4 t = __ldcs(p + static_cast<size_t>(s) * q);
+                    a.x = __fadd_rn(a.x, t.x); a.y = __fadd_rn(a.y, t.y);
+                    a.z = __fadd_rn(a.z, t.z); a.w = __fadd_rn(a.w, t.w);
+                }
+                store_facc<OUT>(C, dst, a.x, ep); store_facc<OUT>(C, dst + 1, a.y, ep);
+                store_facc<OUT>(C, dst + 2, a.z, ep); store_facc<OUT>(C, dst + 3, a.w, ep);
+            }
+        }
+        return;
+    }
+    for (size_t i = first; i < mn; i += step) {
         const size_t col = i / static_cast<size_t>(m), row = i - col * static_cast<size_t>(m);
         const size_t dst = row + col * static_cast<size_t>(ldc);
         if constexpr (OUT == OUT_I32) {
@@ -918,19 +948,21 @@ __global__ void k_splitk_reduce(const void *ws, int parts, int m, int n, void *C
 
 // K slices for a single GEMM whose 128 x 256 tiles fill less than half the SMs but whose K loop is long:
 // the largest power of two S <= 32 that divides the K stages, leaves every slice >= 16 stages and keeps
-// S x tiles within the SM count. 1 = no split. The slices run as a strided batch of the tensor-core kernel
-// into a handle workspace of S partial C (f32, or s32 for INT8), then k_splitk_reduce adds them in order.
-// 512 x 512 x 16384: 8 tiles on 148 SMs become 16 slices x 8 tiles.
+// S x pair tiles within the SM pairs. 1 = no split. The slices run as a strided batch of the tensor-core
+// kernel on the pair tile (with every SM busy the 1-SM tile's operand traffic saturates L2) into a handle
+// workspace of S partial C (f32, or s32 for INT8), then k_splitk_reduce adds them in order.
+// 512 x 512 x 16384: 4 pair tiles on 74 pairs become 16 slices x 4 tiles.
 static int splitk_parts(const Context &ctx, const GemmDesc &d) {
     if (d.batch != 1 || d.algo >= 0 || d.in_kind == IN_TF32 || !ctx.may_allocate || d.m <= BM) return 1;
     const int bk = BK_BYTES / static_cast<int>(in_elem_size(d.in_kind));
     if (d.k % bk != 0) return 1;
     const long long kb = d.k / bk;
-    const long long tiles = static_cast<long long>((d.m + BM - 1) / BM) * ((d.n + BN - 1) / BN);
+    const long long tiles1 = static_cast<long long>((d.m + BM - 1) / BM) * ((d.n + BN - 1) / BN);
+    const long long tiles2 = static_cast<long long>((d.m + 2 * BM - 1) / (2 * BM)) * ((d.n + BN - 1) / BN);
     const long long sms = ctx.sm_count > 0 ? ctx.sm_count : 148;
-    if (2 * tiles > sms) return 1;
+    if (2 * tiles1 > sms) return 1;
     int s = 1;
-    while (s < 32 && 2 * s * tiles <= sms && kb % (2 * s) == 0 && kb / (2 * s) >= 16) s *= 2;
+    while (s < 32 && 2 * s * tiles2 <= sms / 2 && kb % (2 * s) == 0 && kb / (2 * s) >= 16) s *= 2;
     return s;
 }
 
@@ -977,6 +1009,7 @@ cudaError_t launch_tc(Context &ctx, const GemmDesc &d) {
     p.ldc = d.m;
     p.stride_c = static_cast<long long>(mn);
     p.ep = Epilogue{1.0f, 0.0f, 1, 0, 1, 1};
+    p.algo = 1;  // pair tile
     cudaError_t e = launch_tc_one(ctx, p);
     if (e != cudaSuccess) return e;
     const int threads = 256;
