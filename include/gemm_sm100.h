@@ -208,6 +208,16 @@ gs_status gs_plan_gemm_strided_batched_ex(int transa, int transb, int m, int n, 
                                           long long strideB, const void *C, int Ctype, int ldc, long long strideC,
                                           int batchCount, int computeType, uint32_t *kernel);
 
+/* The tensor-core tile and K split a strided-batched typed GEMM of this shape
+ * would use on a device with sm_count SMs, assuming tight leading dimensions
+ * and 16-byte aligned operands: *tile = 1 (1-SM 128x256), 2 (2-SM 256x256
+ * pair) or 3 (2-SM 256x512 wide pair), or 0 for a no-op; *k_slices = the
+ * number of K slices (1 = no split-K). FP32 types (FFMA or the FAST_TF32
+ * split) return GS_STATUS_NOT_SUPPORTED. Pure host logic, for tests and
+ * capacity planning. */
+gs_status gs_plan_tile(int transa, int transb, int m, int n, int k, int Atype, int Ctype, int computeType,
+                       int batchCount, int algo, int sm_count, int *tile, int *k_slices);
+
 /* Largest batchCount gs_gemm_batched_ex_noalloc accepts. */
 #define GS_NOALLOC_MAX_BATCH 256
 

@@ -481,6 +481,30 @@ gs_status gs_plan_gemm_strided_batched_ex(int transa, int transb, int m, int n, 
     return st;
 }
 
+gs_status gs_plan_tile(int transa, int transb, int m, int n, int k, int Atype, int Ctype, int computeType,
+                       int batchCount, int algo, int sm_count, int *tile, int *k_slices) {
+    if (!tile || !k_slices || sm_count < 2) return GS_STATUS_INVALID_VALUE;
+    *tile = 0;
+    *k_slices = 1;
+    // tight leading dimensions of the stored operands (column-major)
+    const int lda = std::max(1, transa ? k : m), ldb = std::max(1, transb ? n : k), ldc = std::max(1, m);
+    GemmDesc d{};
+    std::string why;
+    gs_status st = check_shape_core(transa, transb, m, n, k, lda, ldb, ldc, batchCount, &d, &why);
+    if (st != GS_STATUS_SUCCESS) return st;
+    TypedArgs t;
+    st = decode_types(Atype, Atype, Ctype, computeType, &t);
+    if (st != GS_STATUS_SUCCESS) return st;
+    if (t.in == IN_F32) return GS_STATUS_NOT_SUPPORTED;  // FFMA (or the FAST_TF32 split): not a tile of this kernel
+    if (t.in == IN_I8 && k > 131071) return GS_STATUS_NOT_SUPPORTED;
+    if (m == 0 || n == 0 || k == 0 || batchCount == 0) return GS_STATUS_SUCCESS;
+    d.in_kind = t.in;
+    d.out_kind = t.out;
+    d.algo = algo;
+    plan_tc_tile(d, sm_count, tile, k_slices);
+    return GS_STATUS_SUCCESS;
+}
+
 gs_status gs_gemm_ex(gs_handle h, int transa, int transb, int m, int n, int k, const void *alpha, const void *A,
                      int Atype, int lda, const void *B, int Btype, int ldb, const void *beta, void *C, int Ctype, int ldc,
                      int computeType, int algo) {

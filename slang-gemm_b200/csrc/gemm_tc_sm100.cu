@@ -970,6 +970,21 @@ static int splitk_parts(const Context &ctx, const GemmDesc &d) {
 
 static cudaError_t launch_tc_one(Context &ctx, const GemmDesc &d);
 
+void plan_tc_tile(const GemmDesc &d, int sm_count, int *tile, int *k_slices) {
+    using namespace tc;
+    Context c;
+    c.sm_count = sm_count;
+    const int parts = splitk_parts(c, d);
+    GemmDesc p = d;
+    if (parts > 1) {
+        p.k = d.k / parts;
+        p.batch = parts;
+        p.algo = 1;
+    }
+    *k_slices = parts;
+    *tile = choose_shape(c, p);
+}
+
 cudaError_t launch_tc(Context &ctx, const GemmDesc &d) {
     using namespace tc;
     const int parts = splitk_parts(ctx, d);

@@ -134,6 +134,8 @@ gs_status plan_gemm(const GemmDesc &d, Plan *plan, std::string *why);
 
 // Launchers (return cudaSuccess or the launch error).
 cudaError_t launch_tc(Context &ctx, const GemmDesc &d);
+// Tile (1 = 1-SM 128x256, 2 = pair 256x256, 3 = wide 256x512) and K slices a tensor-core call would use.
+void plan_tc_tile(const GemmDesc &d, int sm_count, int *tile, int *k_slices);
 // FAST_TF32 f32 GEMM on the tensor cores: splits A and B into tf32-exact
 // high/low parts and runs one kind::tf32 GEMM over the concatenated K.
 cudaError_t launch_tf32(Context &ctx, const GemmDesc &d);

@@ -131,6 +131,7 @@ def _load() -> ctypes.CDLL:
         "gs_gemm_batched_ex": (st, [vp, i, i, i, i, i, vp, vp, i, i, vp, i, i, vp, vp, i, i, i, i, i]),
         "gs_plan_gemm_strided_batched_ex": (st, [i, i, i, i, i, vp, i, i, ll, vp, i, i, ll, vp, i, i, ll, i, i,
                                                  ctypes.POINTER(u32)]),
+        "gs_plan_tile": (st, [i, i, i, i, i, i, i, i, i, i, i, ctypes.POINTER(i), ctypes.POINTER(i)]),
         "gs_host_gemm_ex": (st, [vp, ctypes.POINTER(ExDesc)]),
         "gs_host_gemm_batched_ex": (st, [vp, ctypes.POINTER(PtrBatchedDesc)]),
         "gs_plan_shards": (st, [ll, i, ll, ctypes.POINTER(ll)]),
@@ -198,6 +199,18 @@ def plan_gemm(transa, transb, m, n, k, A, atype, lda, stride_a, B, btype, ldb, s
     s = _lib.gs_plan_gemm_strided_batched_ex(transa, transb, m, n, k, A, atype, lda, stride_a, B, btype, ldb,
                                              stride_b, C, ctype, ldc, stride_c, batch, compute, ctypes.byref(kern))
     return s, kern.value
+
+
+TILE_1SM, TILE_PAIR, TILE_WIDE = 1, 2, 3
+
+
+def plan_tile(transa, transb, m, n, k, atype, ctype, compute, batch=1, algo=GEMM_DEFAULT, sm_count=148):
+    """gs_plan_tile: (status, tile, k_slices) a tensor-core call of this shape would use (tile 1 = 1-SM
+    128x256, 2 = pair 256x256, 3 = wide 256x512; k_slices > 1 = split-K). Pure host logic."""
+    tile, parts = ctypes.c_int(0), ctypes.c_int(0)
+    s = _lib.gs_plan_tile(transa, transb, m, n, k, atype, ctype, compute, batch, algo, sm_count, ctypes.byref(tile),
+                          ctypes.byref(parts))
+    return s, tile.value, parts.value
 
 
 def _ptr(x) -> int | None:
