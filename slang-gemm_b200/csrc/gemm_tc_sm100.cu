@@ -906,10 +906,19 @@ __global__ void k_splitk_reduce(const void *ws, int parts, int m, int n, void *C
         for (size_t v = first; v < q; v += step) {
             const size_t i = 4 * v, col = i / static_cast<size_t>(m), row = i - col * static_cast<size_t>(m);
             const size_t dst = row + col * static_cast<size_t>(ldc);
+            // Loads go out four slices at a time, ahead of their adds (the sum stays in slice order).
             if constexpr (OUT == OUT_I32) {
                 const int4 *p = static_cast<const int4 *>(ws) + v;
                 int4 a = make_int4(0, 0, 0, 0);
-                for (int s = 0; s < parts; ++s) {
+                int s = 0;
+                for (; s + 4 <= parts; s += 4) {
+                    int4 t[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) t[j] = __ldcs(p + static_cast<size_t>(s + j) * q);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) { a.x += t[j].x; a.y += t[j].y; a.z += t[j].z; a.w += t[j].w; }
+                }
+                for (; s < parts; ++s) {
                     const int4 t = __ldcs(p + static_cast<size_t>(s) * q);
                     a.x += t.x; a.y += t.y; a.z += t.z; a.w += t.w;
                 }
@@ -918,7 +927,18 @@ __global__ void k_splitk_reduce(const void *ws, int parts, int m, int n, void *C
             } else {
                 const float4 *p = static_cast<const float4 *>(ws) + v;
                 float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                for (int s = 0; s < parts; ++s) {
+                int s = 0;
+                for (; s + 4 <= parts; s += 4) {
+                    float4 t[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) t[j] = __ldcs(p + static_cast<size_t>(s + j) * q);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        a.x = __fadd_rn(a.x, t[j].x); a.y = __fadd_rn(a.y, t[j].y);
+                        a.z = __fadd_rn(a.z, t[j].z); a.w = __fadd_rn(a.w, t[j].w);
+                    }
+                }
+                for (; s < parts; ++s) {
                     const float4 t = __ldcs(p + static_cast<size_t>(s) * q);
                     a.x = __fadd_rn(a.x, t.x); a.y = __fadd_rn(a.y, t.y);
                     a.z = __fadd_rn(a.z, t.z); a.w = __fadd_rn(a.w, t.w);
