@@ -853,7 +853,9 @@ static TcArgs make_args(Context &ctx, const GemmDesc &d, int shape) {
 //    (1024^3, 2048^3, 512 x 512 x 16384);
 //  - with at most 4 K stages the call is all epilogue and the wide tile, whose
 //    16 epilogue warps drain C fastest, is taken (INT8 8192 x 4096 x 256:
-//    1.3x ahead of the pair tile).
+//    1.3x ahead of the pair tile);
+//  - for 16-bit operands with 5-15 K stages the wide tile's cost carries its
+//    exposed accumulator drain, (stages + 2) / stages.
 // Against the earlier rule (wide tile for >= 32 K stages or below the
 // tensor / HBM ridge) this took the sweep's geometric-mean loss against the
 // best tile from 9.7 % to 0.4 %; every configuration of the north star keeps
@@ -882,7 +884,12 @@ static int choose_shape_any(const GemmDesc &d, long long pairs) {
     const int k_blocks = static_cast<int>(cdiv(d.k, BK_BYTES / es));
     if (d.n > BN && k_blocks <= 4) return 3;
     const double c1 = static_cast<double>(r1) / 0.86, c2 = static_cast<double>(r2) / 0.91;
-    const double c3 = 2.0 * static_cast<double>(r3);
+    double c3 = 2.0 * static_cast<double>(r3);
+    // 16-bit operands with fewer than 16 K stages: the wide tile's single accumulator leaves about two stages'
+    // worth of drain exposed per tile (batched 512^3 x 64 and 512 x 1024 x 512 x 96 ran 8-17 % faster on the
+    // pair tile; 4096^2 x 512 and 8192 x 2048 x 512 2 % slower).
+    if ((d.in_kind == IN_F16 || d.in_kind == IN_BF16) && k_blocks < 16)
+        c3 *= (static_cast<double>(k_blocks) + 2.0) / static_cast<double>(k_blocks);
     if (c3 <= c2 && c3 <= c1) return 3;
     return c1 < c2 ? 1 : 2;
 }

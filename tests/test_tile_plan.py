@@ -39,6 +39,13 @@ def test_small_batched_problems_take_the_pair_tile(m, n, k, batch):
     assert plan(m, n, k, batch) == (gs.TILE_PAIR, 1)
 
 
+@pytest.mark.parametrize("m,n,k,batch", [(512, 512, 512, 64), (512, 512, 768, 64), (512, 1024, 512, 96)])
+def test_16bit_short_k_batches_take_the_pair_tile(m, n, k, batch):
+    """5-15 K stages of 16-bit operands: the wide tile's exposed drain tips these to the pair tile."""
+    assert plan(m, n, k, batch) == (gs.TILE_PAIR, 1)
+    assert plan(m, n, k, batch, at=BF16, ct=BF16)[0] == gs.TILE_PAIR
+
+
 def test_short_k_takes_the_wide_tile():
     assert plan(8192, 4096, 256, at=I8, ct=I32, comp=C32I) == (gs.TILE_WIDE, 1)
     assert plan(1024, 1024, 256, 64, at=I8, ct=I32, comp=C32I) == (gs.TILE_WIDE, 1)
