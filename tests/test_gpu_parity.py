@@ -260,20 +260,22 @@ def test_sgemm_strided_batched(handle):
 
 # ---- split-K: long-K single GEMMs whose tiles fill under half the SMs ----------
 
-@pytest.mark.parametrize("dt,ct,op_a,op_b,m,n,k,alpha,beta", [
-    (gs.R_16F, gs.R_32F, 0, 0, 512, 512, 16384, 1.0, 0.0),        # 8 tiles: 16 slices of 1024
-    (gs.R_16BF, gs.R_16BF, 1, 0, 512, 512, 16384, 0.75, -0.5),   # bf16 output rounded once, after the sum
-    (gs.R_8I, gs.R_32I, 0, 1, 384, 640, 8192, 2.0, -1.0),        # INT8: exact s32 sums, clamped epilogue
-    (gs.R_16F, gs.R_16F, 1, 1, 264, 200, 8192, 1.25, 0.5),       # ragged M and N, f16 output
-    (gs.R_16F, gs.R_32F, 0, 0, 1024, 1024, 4096, 1.5, 0.25),     # 32 tiles: 4 slices
+@pytest.mark.parametrize("dt,ct,op_a,op_b,m,n,k,alpha,beta,pad", [
+    (gs.R_16F, gs.R_32F, 0, 0, 512, 512, 16384, 1.0, 0.0, (0, 0, 0)),        # 16 slices of 1024
+    (gs.R_16BF, gs.R_16BF, 1, 0, 512, 512, 16384, 0.75, -0.5, (0, 0, 0)),   # bf16 output rounded once, after the sum
+    (gs.R_8I, gs.R_32I, 0, 1, 384, 640, 8192, 2.0, -1.0, (0, 0, 0)),        # INT8: exact s32 sums, clamped epilogue
+    (gs.R_16F, gs.R_16F, 1, 1, 264, 200, 8192, 1.25, 0.5, (0, 0, 0)),       # ragged M and N, f16 output
+    (gs.R_16F, gs.R_32F, 0, 0, 1024, 1024, 4096, 1.5, 0.25, (0, 0, 0)),     # 4 slices
+    (gs.R_16F, gs.R_32F, 0, 1, 512, 512, 16384, 1.0, 0.5, (8, 16, 3)),      # padded lda / ldb / ldc, beta != 0
+    (gs.R_8I, gs.R_32I, 1, 0, 512, 256, 16384, 3.0, 2.0, (16, 32, 5)),      # padded, INT8, ldc not a multiple of 4
 ])
-def test_splitk_matches_oracle(handle, dt, ct, op_a, op_b, m, n, k, alpha, beta):
+def test_splitk_matches_oracle(handle, dt, ct, op_a, op_b, m, n, k, alpha, beta, pad):
     """Long-K GEMMs with few output tiles split K into slices that run as a strided batch of the tensor-core
     kernel into a workspace; a second kernel adds the slices in order and applies alpha / beta with the
     reference's rounding. Bit-exact for INT8, within the type's tolerance otherwise, bytes outside C kept."""
     comp = gs.COMPUTE_32I if dt == gs.R_8I else gs.COMPUTE_32F
-    kern = run_case(handle, dt, op_a, op_b, m, n, k, alpha=alpha, beta=beta, ct=ct, seed=m + n + k, comp=comp,
-                    expect_kernel=TC[dt])
+    kern = run_case(handle, dt, op_a, op_b, m, n, k, alpha=alpha, beta=beta, ct=ct, pad=pad, seed=m + n + k,
+                    comp=comp, expect_kernel=TC[dt])
     assert kern & gs.KERNEL_REDUCE, kern
 
 
