@@ -1,7 +1,7 @@
 """The device entry points inside CUDA graphs: after one warm-up call (which
 sets kernel attributes and allocates the handle's tensor-map buffer), a call
 captured into a graph and replayed must give the same bits as the direct
-call, for every kernel family (tensor-core single / strided / pointer-array,
+call, for every kernel family (tensor-core single / strided / pointer-array / split-K,
 FFMA data-parallel and stream-K, the FAST_TF32 split + tf32 GEMM, CUDA-core
 fallback, k = 0)."""
 import numpy as np
@@ -27,6 +27,7 @@ def _dev(x):
     (gs.R_16F, 64, 64, 0, 1, 0, False, -1),         # k == 0: beta only
     (gs.R_32F, 1024, 512, 1100, 1, 0, False, -1),   # FAST_TF32: split kernels + chunked kind::tf32 GEMM
     (gs.R_32F, 1600, 1100, 1030, 2, 0, False, -1),  # FFMA stream-K (234 tiles on 296 slots): workspace, counters
+    (gs.R_16F, 512, 512, 16384, 1, 0, False, -1),   # tensor-core split-K: 16 slices into a workspace + reduction
 ])
 def test_graph_replay_matches_direct_call(dt, m, n, k, batch, lda_pad, ptr, algo):
     rng = np.random.default_rng(m + n + k)
