@@ -946,6 +946,101 @@ def run_manifest(args):
     return 0
 
 
+# Shapes of the tile-choice sweep (M, N, K, batch) and of the split-K comparison.
+TILE_SWEEP_SHAPES = [
+    (8192, 8192, 8192, 1), (4096, 4096, 4096, 1), (2048, 2048, 2048, 1), (8192, 8192, 1024, 1), (4096, 4096, 1024, 1),
+    (8192, 1024, 8192, 1), (1024, 8192, 8192, 1), (3000, 3000, 3000, 1), (6144, 6144, 2048, 1), (2048, 8192, 4096, 1),
+    (8192, 2048, 512, 1), (1536, 1536, 1536, 1), (512, 512, 16384, 1), (16384, 4096, 1024, 1), (1024, 1024, 1024, 1),
+    (512, 512, 1024, 256), (2048, 2048, 2048, 64), (1024, 1024, 1024, 32), (256, 256, 4096, 128), (768, 768, 768, 64),
+    (4096, 4096, 256, 8), (2048, 2048, 1536, 16), (2560, 2560, 2560, 1), (3072, 3072, 1024, 1), (1024, 4096, 2048, 1),
+    (4096, 2048, 2048, 1), (1024, 1024, 4096, 1), (2048, 2048, 512, 1), (512, 512, 512, 64), (1024, 1024, 256, 64),
+    (2048, 1024, 1024, 16), (384, 384, 1024, 128), (1280, 1280, 1280, 8), (8192, 4096, 256, 1), (512, 512, 768, 64),
+    (512, 1024, 512, 96)]
+SPLITK_SHAPES = [(512, 512, 16384, 1), (1024, 1024, 4096, 1), (1024, 1024, 8192, 1), (256, 1024, 32768, 1),
+                 (2048, 512, 8192, 1), (768, 768, 12288, 1)]
+
+
+def run_tile_sweep(args) -> int:
+    """Every tensor-core tile against the automatic choice, and cuBLAS, over a list of shapes (op N/N, alpha 1,
+    beta 0). The five calls of a shape (algo -1 automatic, 0 = 1-SM 128x256, 1 = pair 256x256, 2 = wide 256x512,
+    cuBLAS) are timed in turn, 7 times, each time as a run of back-to-back calls of about 2 ms after a 256 MiB L2
+    flush (the event clock ticks in ~2 us steps here, so short calls are not timed one by one); the medians of
+    the per-call times are printed, one JSON line per shape, with whether the automatic call split K."""
+    import torch
+
+    import cublas_ref
+    import gemm_sm100 as gs
+
+    torch.cuda.set_device(0)
+    h = gs.Handle()
+    cb = cublas_ref.Cublas(stream=torch.cuda.current_stream())
+    flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device="cuda")
+
+    def run_of(fn, r):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(r):
+            fn()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / r
+
+    shapes = SPLITK_SHAPES if args.tile_sweep == "splitk" else TILE_SWEEP_SHAPES
+    if args.sweep_shapes:
+        shapes = [tuple(int(v) for v in x.split("x")) + ((1,) if x.count("x") == 2 else ()) for x in
+                  args.sweep_shapes.split(",")]
+    types = {"f16": (gs.R_16F, gs.R_32F, gs.COMPUTE_32F), "bf16": (gs.R_16BF, gs.R_16BF, gs.COMPUTE_32F),
+             "i8": (gs.R_8I, gs.R_32I, gs.COMPUTE_32I)}
+    for dname in args.sweep_dtypes.split(","):
+        at, ct, comp = types[dname]
+        for m, n, k, b in shapes:
+            if at == gs.R_8I and (m % 16 or k % 16):
+                continue  # not TMA-addressable: the CUDA-core path, no tile to compare
+            g = torch.Generator(device="cuda").manual_seed(m + n + k + b)
+            if at == gs.R_8I:
+                A = torch.randint(-128, 128, (b * m * k,), generator=g, device="cuda", dtype=torch.int16).to(torch.int8)
+                B = torch.randint(-128, 128, (b * k * n,), generator=g, device="cuda", dtype=torch.int16).to(torch.int8)
+                C = torch.zeros(b * m * n, dtype=torch.int32, device="cuda")
+            else:
+                tdt = torch.float16 if at == gs.R_16F else torch.bfloat16
+                A = torch.randn(b * m * k, generator=g, device="cuda").to(tdt)
+                B = torch.randn(b * k * n, generator=g, device="cuda").to(tdt)
+                C = torch.zeros(b * m * n, dtype=torch.float32 if ct == gs.R_32F else tdt, device="cuda")
+            C2 = C.clone()
+
+            def ours(algo):
+                return lambda: h.gemm_strided_batched_ex(0, 0, m, n, k, 1, A, at, m, m * k, B, at, k, k * n, 0, C, ct,
+                                                         m, m * n, b, comp, algo=algo)
+
+            fns = [ours(-1), ours(0), ours(1), ours(2),
+                   lambda: cb.gemm_strided_batched_ex(0, 0, m, n, k, 1, A, at, m, m * k, B, at, k, k * n, 0, C2, ct,
+                                                      m, m * n, b, comp)]
+            for f in fns:
+                f()
+                f()
+            torch.cuda.synchronize()
+            r = max(3, min(200, int(2.0 / max(run_of(fns[0], 3), 1e-3))))
+            ts = [[] for _ in fns]
+            for _ in range(7):
+                for i, f in enumerate(fns):
+                    ts[i].append(run_of(f, r))
+            med = [sorted(x)[3] for x in ts]
+            fns[0]()
+            kern = h.last_kernels()
+            st, tile, parts = gs.plan_tile(0, 0, m, n, k, at, ct, comp, batch=b)
+            best = min(med[1:4])
+            emit({"mode": "tile-sweep", "dt": dname, "m": m, "n": n, "k": k, "batch": b,
+                  "auto_ms": round(med[0], 5), "tile_1sm_ms": round(med[1], 5), "tile_pair_ms": round(med[2], 5),
+                  "tile_wide_ms": round(med[3], 5), "cublas_ms": round(med[4], 5),
+                  "auto_tile": tile, "auto_k_slices": parts, "split_k": bool(kern & gs.KERNEL_REDUCE),
+                  "best_tile": 1 + min(range(3), key=lambda i: med[1 + i]), "auto_over_best": round(med[0] / best, 4),
+                  "auto_over_cublas": round(med[0] / med[4], 4)})
+            del A, B, C, C2
+            torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     global _RESULT_FD
     sys.stdout.flush()
@@ -979,6 +1074,11 @@ def main():
                          "2 = 256x512 pair; -1 = automatic)")
     ap.add_argument("--sustained", type=float, default=0.0, metavar="SECONDS",
                     help="instead of the contract line: power-capped steady state of this library vs cuBLAS")
+    ap.add_argument("--tile-sweep", default=None, choices=["tiles", "splitk"],
+                    help="instead of the contract line: every tensor-core tile against the automatic choice and "
+                         "cuBLAS over the sweep's shapes ('tiles') or the split-K shapes ('splitk')")
+    ap.add_argument("--sweep-shapes", default=None, help="--tile-sweep shapes, MxNxK[xBATCH] comma-separated")
+    ap.add_argument("--sweep-dtypes", default="f16,i8", help="--tile-sweep input types: f16, bf16, i8")
     rows = ap.add_argument_group("manifest rows (the reference's JSONL benchmark CLI; any of these selects it)")
     rows.add_argument("--manifest", default=None, help="'all': every API/op/type case (bench/gemm_perf.zig:91)")
     rows.add_argument("--sizes", default=None, help="comma-separated square sizes (default 512,1024,2048)")
@@ -1005,6 +1105,8 @@ def main():
         args.fail_on_regression or args.only_cublas_supported or args.tile_compatible_only
     if row_mode:
         sys.exit(run_manifest(args))
+    if args.tile_sweep:
+        sys.exit(run_tile_sweep(args))
     if args.sustained:
         run_sustained(args, args.config)
         return

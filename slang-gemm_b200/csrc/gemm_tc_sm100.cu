@@ -975,7 +975,7 @@ __global__ void k_splitk_reduce(const void *ws, int parts, int m, int n, void *C
 
 // K slices for a single GEMM whose 128 x 256 tiles fill less than half the SMs but whose K loop is long:
 // the largest power of two S <= 32 that divides the K stages, leaves every slice >= 16 stages and keeps
-// S x pair tiles within the SM pairs. 1 = no split. The slices run as a strided batch of the tensor-core
+// S x pair tiles within the SM pairs, if it is at least 4. 1 = no split. The slices run as a strided batch of the tensor-core
 // kernel on the pair tile (with every SM busy the 1-SM tile's operand traffic saturates L2) into a handle
 // workspace of S partial C (f32, or s32 for INT8), then k_splitk_reduce adds them in order.
 // 512 x 512 x 16384: 4 pair tiles on 74 pairs become 16 slices x 4 tiles.
@@ -990,7 +990,7 @@ static int splitk_parts(const Context &ctx, const GemmDesc &d) {
     if (2 * tiles1 > sms) return 1;
     int s = 1;
     while (s < 32 && 2 * s * tiles2 <= sms / 2 && kb % (2 * s) == 0 && kb / (2 * s) >= 16) s *= 2;
-    return s;
+    return s >= 4 ? s : 1;  // two slices do not pay for the reduction (INT8 1024^2 x 4096: 7 % slower)
 }
 
 }  // namespace tc

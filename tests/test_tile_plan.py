@@ -78,6 +78,7 @@ def test_split_k_is_not_taken():
     assert plan(512, 512, 16384, batch=2)[1] == 1   # batched calls
     assert plan(4096, 4096, 16384)[1] == 1          # enough tiles to fill the GPU
     assert plan(1024, 1024, 1024)[1] == 1           # too few K stages per slice
+    assert plan(1024, 1024, 4096, at=I8, ct=I32, comp=C32I)[1] == 1  # two slices would not pay for the reduction
 
 
 def test_smaller_gpu_scales_the_rounds():
