@@ -138,3 +138,16 @@ def test_reference_arm_line_describes_one_whole_step():
 def test_cli_rejects_unknown_config_in_a_list():
     p = _run("--config", "c3-f16-nn,nope")
     assert p.returncode != 0 and "nope" in p.stderr
+
+
+def test_tile_sweep_shape_lists_match_the_rule():
+    """The shapes `bench.py --tile-sweep` times: well-formed, and every split-K shape is one the library splits
+    (at least 4 slices), so the split-K profile measures the split path."""
+    import gemm_sm100 as gs
+
+    for shapes in (bench.TILE_SWEEP_SHAPES, bench.SPLITK_SHAPES):
+        assert shapes and all(len(s) == 4 and all(isinstance(v, int) and v > 0 for v in s) for s in shapes)
+    for m, n, k, b in bench.SPLITK_SHAPES:
+        for at, ct, comp in ((gs.R_16F, gs.R_32F, gs.COMPUTE_32F), (gs.R_16BF, gs.R_16BF, gs.COMPUTE_32F)):
+            st, tile, parts = gs.plan_tile(0, 0, m, n, k, at, ct, comp, batch=b)
+            assert st == gs.STATUS_SUCCESS and parts >= 4, (m, n, k, parts)
