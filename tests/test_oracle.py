@@ -416,3 +416,39 @@ def test_hgemm_rounds_to_f16():
                 s = F32(s + F32(ad[row + kk * m] * bd[kk + col * k]))
             v = F32(F32(F32(1.5) * s) + F32(F32(-0.5) * cd[row + col * m]))
             assert got[row + col * m] == np.array([v], F32).astype(np.float16).view(np.uint16)[0]
+
+
+@pytest.mark.parametrize("op_a", [0, 1])
+@pytest.mark.parametrize("op_b", [0, 1])
+def test_int8_checksum_identities_and_layout_duality_are_exact(op_a, op_b):
+    """The size-independent properties the full-size GPU tests check, pinned on the oracle itself: with
+    alpha 1 and beta 0 an INT8 GEMM is exact, so the column sums of C equal (1^T op(A)) op(B) and the row
+    sums equal op(A) (op(B) 1) in int64; and a row-major call equals the column-major call on the same
+    bytes with the operands swapped (C^T = op(B)^T op(A)^T), element for element."""
+    rng = np.random.default_rng(20 + 2 * op_a + op_b)
+    m, n, k = 23, 17, 300  # |sums| reach 128 * 128 * 300, far beyond int16
+    ar, ac = (m, k) if op_a == 0 else (k, m)
+    br, bc = (k, n) if op_b == 0 else (n, k)
+    a = rng.integers(-128, 128, ar * ac).astype(np.int8)
+    b = rng.integers(-128, 128, br * bc).astype(np.int8)
+    c = np.zeros(m * n, np.int32)
+    assert orc.gemm_ex(op_a, op_b, m, n, k, 1.0, a, orc.R_8I, ar, b, orc.R_8I, br, 0.0, c, orc.R_32I, m,
+                       compute_type=72) == orc.OK
+    am = a.astype(np.int64).reshape(ac, ar).T  # stored column-major, ar x ac
+    bm = b.astype(np.int64).reshape(bc, br).T
+    opa, opb = (am if op_a == 0 else am.T), (bm if op_b == 0 else bm.T)
+    cm = c.astype(np.int64).reshape(n, m).T
+    np.testing.assert_array_equal(cm.sum(axis=0), opa.sum(axis=0) @ opb)
+    np.testing.assert_array_equal(cm.sum(axis=1), opa @ opb.sum(axis=1))
+    # The same matrices stored row-major (leading dimension = stored columns) give the same C, row-major.
+    a_rm = np.ascontiguousarray(am).astype(np.int8).ravel()
+    b_rm = np.ascontiguousarray(bm).astype(np.int8).ravel()
+    c_rm = np.zeros(m * n, np.int32)
+    assert orc.gemm_ex(op_a, op_b, m, n, k, 1.0, a_rm, orc.R_8I, ac, b_rm, orc.R_8I, bc, 0.0, c_rm,
+                       orc.R_32I, n, compute_type=72, layout=orc.ROW_MAJOR) == orc.OK
+    np.testing.assert_array_equal(c_rm.reshape(m, n), cm)
+    # Column-major bytes of A and B read as the swapped call C^T = op(B)^T op(A)^T give C^T column-major.
+    c_sw = np.zeros(m * n, np.int32)
+    assert orc.gemm_ex(1 - op_b, 1 - op_a, n, m, k, 1.0, b, orc.R_8I, br, a, orc.R_8I, ar, 0.0, c_sw, orc.R_32I,
+                       n, compute_type=72) == orc.OK
+    np.testing.assert_array_equal(c_sw.astype(np.int64).reshape(m, n), cm)
