@@ -151,3 +151,25 @@ def test_tile_sweep_shape_lists_match_the_rule():
         for at, ct, comp in ((gs.R_16F, gs.R_32F, gs.COMPUTE_32F), (gs.R_16BF, gs.R_16BF, gs.COMPUTE_32F)):
             st, tile, parts = gs.plan_tile(0, 0, m, n, k, at, ct, comp, batch=b)
             assert st == gs.STATUS_SUCCESS and parts >= 4, (m, n, k, parts)
+
+
+def test_reference_arm_under_torchrun_world_two_prints_once():
+    """The driver launches the reference arm like our own arm for N > 1 (torchrun, one process per GPU):
+    rank 0 alone runs the sample and prints the line, with rank 0's share in `config`; rank 1 exits 0."""
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), os.path.join(ROOT, "bench.py"),
+           "--impl", "reference", "--gpus", "2", "--steps", "3", "--warmup", "3", "--ref-seconds", "1.5"]
+    p = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env, cwd=ROOT)
+    assert p.returncode == 0, p.stderr[-2000:]
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
+    # weak scaling: two ranks' worth of columns, rank 0 holding the first 8192 of 16384
+    assert d["config"]["per_rank"]["n"] == 8192
